@@ -1,0 +1,372 @@
+/*
+ * matrixman_b200.h -- C ABI of libmatrixman_b200.so, the B200 (sm_100a) execution
+ * runtime behind the `matrixman` PrivateUse1 tensor-op backend.
+ *
+ * This boundary replaces MatrixMan's legacy-CUDA execution runtime
+ * (drivers/matrixman/backends/cuda/gpumatrix.py, class CudaExecutionBackend,
+ * gpumatrix.py:4549-5900), which the Python backend façade
+ * (drivers/matrixman/backends/cuda/backend.py) drives through ctypes with raw
+ * CUdeviceptr values and u32 sizes.  Here every call takes plain pointers,
+ * int64 sizes/strides and an opaque stream handle; no torch type crosses it.
+ *
+ * Conventions
+ *  - Every function returns an int status: MM_OK (0) or an mm_status error code.
+ *    The message of the last failure on the calling thread is returned by
+ *    mm_last_error(); the Python layer maps codes to RuntimeError /
+ *    NotImplementedError / ValueError / MemoryError, mirroring the reference's
+ *    convention of "RuntimeError(<action>: <CUDA_ERROR_NAME> (<message>))"
+ *    (gpumatrix.py:4508-4518).
+ *  - `stream` is a cudaStream_t passed as void*; NULL means the device's runtime
+ *    stream created by mm_init().
+ *  - Tensor descriptors carry the element pointer of logical index [0,...,0]
+ *    (storage offset already applied), rank <= MM_MAX_DIMS, sizes and strides in
+ *    elements.  Strides may be 0 (broadcast/expand) but never negative.
+ *  - All kernels are asynchronous on `stream`.  Waits are bounded polls that
+ *    return MM_ERR_TIMEOUT instead of blocking forever.
+ */
+#ifndef MATRIXMAN_B200_H
+#define MATRIXMAN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MM_MAX_DIMS 6
+#define MM_ABI_VERSION 1
+
+typedef enum mm_status {
+  MM_OK = 0,
+  MM_ERR_INVALID = 1,      /* bad argument (maps to ValueError) */
+  MM_ERR_UNSUPPORTED = 2,  /* unsupported op/dtype/shape (NotImplementedError) */
+  MM_ERR_OOM = 3,          /* device memory exhausted after drain + retry (MemoryError) */
+  MM_ERR_CUDA = 4,         /* CUDA runtime error (RuntimeError) */
+  MM_ERR_TIMEOUT = 5,      /* a bounded wait gave up (TimeoutError) */
+  MM_ERR_STATE = 6         /* runtime not initialised / wrong device (RuntimeError) */
+} mm_status_t;
+
+typedef enum mm_dtype { MM_F32 = 0, MM_I64 = 1 } mm_dtype_t;
+
+typedef enum mm_pool_kind {
+  MM_POOL_ACTIVATION = 0,  /* op outputs: matrixman.config.activation_pool */
+  MM_POOL_SCRATCH = 1,     /* intra-op temporaries: matrixman.config.scratch_pool */
+  MM_POOL_PARAMETER = 2    /* uploaded/prepacked weights: never pooled */
+} mm_pool_kind_t;
+
+typedef enum mm_act {
+  MM_ACT_NONE = 0,
+  MM_ACT_RELU = 1,
+  MM_ACT_SILU = 2,
+  MM_ACT_SIGMOID = 3
+} mm_act_t;
+
+typedef enum mm_unary_op {
+  MM_UNARY_COPY = 0,
+  MM_UNARY_SILU = 1,
+  MM_UNARY_RELU = 2,
+  MM_UNARY_SIGMOID = 3,
+  MM_UNARY_ADD_SCALAR = 4,   /* y = x + a */
+  MM_UNARY_MUL_SCALAR = 5,   /* y = x * a */
+  MM_UNARY_DIV_SCALAR = 6,   /* y = x / a (IEEE division) */
+  MM_UNARY_NEG = 7,
+  MM_UNARY_CLAMP = 8         /* y = min(max(x, a), b) */
+} mm_unary_op_t;
+
+typedef enum mm_binary_op {
+  MM_BINARY_ADD = 0,  /* y = a + alpha*b */
+  MM_BINARY_SUB = 1,  /* y = a - alpha*b */
+  MM_BINARY_MUL = 2,  /* y = a * b */
+  MM_BINARY_DIV = 3   /* y = a / b */
+} mm_binary_op_t;
+
+typedef struct mm_tensor {
+  void* data;
+  int32_t dtype;  /* mm_dtype_t */
+  int32_t ndim;
+  int64_t size[MM_MAX_DIMS];
+  int64_t stride[MM_MAX_DIMS];
+} mm_tensor_t;
+
+typedef struct mm_device_info {
+  char name[256];
+  int32_t cc_major;
+  int32_t cc_minor;
+  int32_t sm_count;
+  int32_t reserved;
+  int64_t total_bytes;
+  int64_t free_bytes;
+} mm_device_info_t;
+
+typedef struct mm_pool_stats {
+  int64_t live_bytes[3];      /* indexed by mm_pool_kind_t */
+  int64_t cached_bytes[3];
+  int64_t pending_bytes[3];
+  int64_t peak_live_bytes[3];
+  int64_t alloc_calls[3];
+  int64_t pool_hits[3];
+  int64_t device_mallocs;
+  int64_t device_frees;
+  int64_t oom_recoveries;
+  int64_t capture_pools;
+} mm_pool_stats_t;
+
+/* Convolution geometry.  Replaces the positional u32 argument list of
+ * CudaExecutionBackend.convolution (gpumatrix.py:5414-5788). */
+typedef struct mm_conv_params {
+  int32_t stride_h, stride_w;
+  int32_t pad_h, pad_w;
+  int32_t dil_h, dil_w;
+  int32_t groups;
+  int32_t act;                 /* mm_act_t applied in the epilogue */
+  int32_t residual_before_act; /* 1: act(conv+bias+res); 0: act(conv+bias)+res */
+  int32_t algo;                /* 0 = auto, 1 = SIMT fp32, 2 = tcgen05 3xTF32 */
+} mm_conv_params_t;
+
+/* ------------------------------------------------------------------------ */
+/* Runtime: errors, devices, streams, events                                 */
+/* ------------------------------------------------------------------------ */
+
+/* ABI version of the loaded library (MM_ABI_VERSION). */
+int mm_abi_version(void);
+
+/* Copy the calling thread's last error message into buf (NUL-terminated).
+ * Replaces gpumatrix.py:4508-4518 (check/CudaError formatting). */
+int mm_last_error(char* buf, size_t n);
+
+/* Number of visible CUDA devices.  Replaces detect_device (gpumatrix.py:4521-4546),
+ * which only ever looked at device 0. */
+int mm_device_count(int* out);
+
+/* Name, compute capability, SM count and memory of a device. */
+int mm_device_info(int device, mm_device_info_t* out);
+
+/* Create the per-device runtime: context, runtime stream, arena.  Idempotent.
+ * Replaces CudaExecutionBackend.__init__ (gpumatrix.py:4552-4764). */
+int mm_init(int device);
+
+/* Synchronise, release every cached block and destroy the runtime stream.
+ * Replaces CudaExecutionBackend.close (gpumatrix.py:4765-4784). */
+int mm_shutdown(int device);
+
+/* Make `device` current for the calling thread. */
+int mm_set_device(int device);
+
+/* The device's runtime stream (created by mm_init). */
+int mm_runtime_stream(int device, void** stream_out);
+
+int mm_stream_create(int device, void** stream_out);
+int mm_stream_destroy(void* stream);
+
+/* Bounded wait for all work on `stream`; MM_ERR_TIMEOUT after timeout_ms
+ * (timeout_ms < 0 waits without limit).  Replaces cuCtxSynchronize at the
+ * readback boundary (gpumatrix.py:4896-4911). */
+int mm_stream_sync(void* stream, int64_t timeout_ms);
+
+/* 1 in *done if every operation on the stream has completed. */
+int mm_stream_query(void* stream, int* done);
+
+int mm_event_create(void** event_out, int timing);
+int mm_event_destroy(void* event);
+int mm_event_record(void* event, void* stream);
+int mm_event_sync(void* event, int64_t timeout_ms);
+int mm_stream_wait_event(void* stream, void* event);
+/* Milliseconds between two recorded events.  Replaces the CUDA-event GPU
+ * timing of gpumatrix.py:4785-4816. */
+int mm_event_elapsed_ms(void* start, void* stop, float* ms);
+
+/* ------------------------------------------------------------------------ */
+/* Caching arena (activation_pool / scratch_pool)                            */
+/* ------------------------------------------------------------------------ */
+
+/* Pool policy.  sync_safe=1: a reused block is ordered after its last use by a
+ * stream-event wait ("safe"); 0: stream-ordered reuse only ("relaxed").
+ * deferred_*=1: released blocks stay pending until their release event has
+ * completed ("deferred"); 0: immediately reusable ("safe").  Maps
+ * matrixman.config sync_policy/activation_pool/scratch_pool (config.py:19-42)
+ * onto the exact-size pool with deferred release of gpumatrix.py:4846-5012. */
+int mm_pool_configure(int device, int sync_safe, int deferred_activation, int deferred_scratch,
+                      int disable_pool);
+
+/* Allocate `bytes` of device memory from pool `kind`.  On exhaustion the arena
+ * synchronises, drains pending/cached blocks and retries once before failing
+ * with MM_ERR_OOM.  Replaces CudaExecutionBackend.allocate / _allocate_driver
+ * (gpumatrix.py:4926-4962, 4913-4923). */
+int mm_alloc(int device, size_t bytes, int kind, void* stream, void** out);
+
+/* Release a block; reuse is ordered after all work queued on `stream`.
+ * Replaces CudaExecutionBackend.free (gpumatrix.py:4965-5001). */
+int mm_free(void* ptr, void* stream);
+
+/* Move completed pending blocks to the cache and cudaFree every cached block.
+ * Replaces _drain_pool (gpumatrix.py:5002-5012). */
+int mm_pool_trim(int device);
+
+int mm_pool_stats(int device, mm_pool_stats_t* out);
+
+/* Test hook: after `n` more successful device allocations, report device OOM
+ * (n < 0 disables).  Environment: MATRIXMAN_TEST_FAIL_ALLOC_AFTER. */
+int mm_debug_fail_alloc_after(int device, int64_t n);
+
+/* Host-backed arena instance with the same policy code, for CPU-only tests of the
+ * pool state machine (no GPU needed).  Events are simulated: a release recorded
+ * at generation g completes once mm_host_arena_complete(g' >= g) is called. */
+int mm_host_arena_create(int64_t capacity_bytes, int deferred, void** arena_out);
+int mm_host_arena_destroy(void* arena);
+int mm_host_arena_alloc(void* arena, size_t bytes, int kind, void** out);
+int mm_host_arena_free(void* arena, void* ptr);
+int mm_host_arena_complete(void* arena, int64_t generation);
+int mm_host_arena_generation(void* arena, int64_t* out);
+int mm_host_arena_fail_after(void* arena, int64_t n);
+int mm_host_arena_stats(void* arena, mm_pool_stats_t* out);
+
+/* ------------------------------------------------------------------------ */
+/* Copies                                                                    */
+/* ------------------------------------------------------------------------ */
+
+/* Host<->device copies.  `sync` = 1 waits (bounded) for completion.  Replace
+ * to_device / from_device (gpumatrix.py:5021-5049). */
+int mm_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream, int sync);
+int mm_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream, int sync);
+int mm_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+/* Copy-engine copy between two devices (NVLink when peer access is enabled). */
+int mm_memcpy_peer(void* dst, int dst_device, const void* src, int src_device, size_t bytes,
+                   void* stream);
+int mm_enable_peer_access(int device, int peer);
+/* Page-locked host buffers for asynchronous transfers. */
+int mm_host_alloc_pinned(size_t bytes, void** out);
+int mm_host_free_pinned(void* ptr);
+
+/* ------------------------------------------------------------------------ */
+/* CUDA graphs (prepared-model execution)                                    */
+/* ------------------------------------------------------------------------ */
+
+/* Begin capturing work queued on `stream`.  Arena allocations made on this
+ * device until mm_graph_capture_end come from a private pool owned by the
+ * graph, so replay never races with eager allocations. */
+int mm_graph_capture_begin(int device, void* stream);
+int mm_graph_capture_end(int device, void* stream, void** graph_out);
+int mm_graph_launch(void* graph, void* stream);
+/* Synchronise and free the graph and its private pool. */
+int mm_graph_destroy(void* graph);
+
+/* ------------------------------------------------------------------------ */
+/* Operators                                                                 */
+/* ------------------------------------------------------------------------ */
+
+/* y = op(x) elementwise, any strides, x and y of equal logical shape (y may
+ * alias x for in-place).  Replaces matrix_sigmoid / silu / matrix_add_scalar /
+ * matrix_div_scalar kernels (gpumatrix.py:581, 4012, 478, 510) and
+ * CudaBackend.{sigmoid,silu,div} (cuda/backend.py:733-796, 1031-1070). */
+int mm_unary(int op, const mm_tensor_t* x, const mm_tensor_t* y, double a, double b, void* stream);
+
+/* y = op(a, b) with broadcasting expressed by 0-strides.  Replaces matrix_add /
+ * matrix_sub / matrix_mul_elementwise (gpumatrix.py:171, 351, 265) and
+ * CudaBackend.{add,sub,mul} (cuda/backend.py:888-1122). */
+int mm_binary(int op, const mm_tensor_t* a, const mm_tensor_t* b, const mm_tensor_t* y,
+              double alpha, void* stream);
+
+/* y[...] = value.  Replaces matrix_fill (gpumatrix.py:728). */
+int mm_fill(const mm_tensor_t* y, double value, void* stream);
+
+/* y[i] = start + i*step over a 1-D tensor.  Replaces matrix_arange (gpumatrix.py:445). */
+int mm_arange(const mm_tensor_t* y, double start, double step, void* stream);
+
+/* y = x for arbitrary strides (materialising copy).  Replaces split_copy /
+ * stack_copy (gpumatrix.py:4049, 652). */
+int mm_copy(const mm_tensor_t* x, const mm_tensor_t* y, void* stream);
+
+/* Concatenate `n` tensors along `dim` into y (one launch per input, each
+ * writing only its own slot).  Replaces cat_copy (gpumatrix.py:4135), which
+ * launched numel(out) threads per input. */
+int mm_cat(const mm_tensor_t* const* inputs, int n, int dim, const mm_tensor_t* y, void* stream);
+
+/* Eval-mode BatchNorm over channel dim 1: y = (x-mean)*rsqrt(var+eps)*w + b.
+ * Replaces batch_norm_inference (gpumatrix.py:3945-4010). */
+int mm_batch_norm(const mm_tensor_t* x, const float* mean, const float* var, const float* weight,
+                  const float* bias, double eps, const mm_tensor_t* y, void* stream);
+
+/* Softmax (log=0) or log-softmax (log=1) along `dim`.  Replaces matrix_softmax
+ * (gpumatrix.py:784-931) and CudaBackend.softmax (cuda/backend.py:1290-1349). */
+int mm_softmax(const mm_tensor_t* x, int dim, int log, const mm_tensor_t* y, void* stream);
+
+/* Generic 2-D max pooling over dims (2,3) of a rank-4 tensor, -inf padding,
+ * NaN-propagating like torch.  Replaces max_pool2d_5x5_s1_p2 (gpumatrix.py:74)
+ * and CudaBackend.max_pool2d (cuda/backend.py:1351-1393), which only accepted
+ * 5x5/s1/p2. */
+int mm_max_pool2d(const mm_tensor_t* x, int kh, int kw, int sh, int sw, int ph, int pw, int dh,
+                  int dw, const mm_tensor_t* y, void* stream);
+
+/* SPPF pooling chain: y1 = pool5(x), y2 = pool5(y1), y3 = pool5(y2) with 5x5/s1/p2
+ * max pooling, computed in one pass (nested 5/9/13 windows).  y1..y3 are
+ * typically channel slices of the SPPF concat buffer.  Fuses the three
+ * max_pool2d_5x5_s1_p2 launches of the reference SPPF path. */
+int mm_sppf_pool(const mm_tensor_t* x, const mm_tensor_t* y1, const mm_tensor_t* y2,
+                 const mm_tensor_t* y3, void* stream);
+
+/* avg_pool2d with torch semantics (count_include_pad, divisor_override <= 0 =
+ * none, ceil_mode handled by the caller through the output size).  Semantics of
+ * the OpenGL-only reference pooling (backends/opengl/ops/pooling.py). */
+int mm_avg_pool2d(const mm_tensor_t* x, int kh, int kw, int sh, int sw, int ph, int pw,
+                  int count_include_pad, int divisor_override, const mm_tensor_t* y, void* stream);
+
+/* Adaptive average pooling over dims (2,3). */
+int mm_adaptive_avg_pool2d(const mm_tensor_t* x, const mm_tensor_t* y, void* stream);
+
+/* Mean (or sum when mean=0) over the dims whose bit is set in dim_mask; y has
+ * the reduced dims with size 1.  Semantics of backends/opengl/ops/reduction.py:136-221. */
+int mm_reduce(const mm_tensor_t* x, uint32_t dim_mask, int mean, const mm_tensor_t* y, void* stream);
+
+/* Nearest-neighbour 2-D upsampling with torch's index rule; scale_h/scale_w > 0
+ * are the user scale factors (source index = floor(dst * (1/scale))), else
+ * input/output size ratios.  Replaces upsample_nearest2d (gpumatrix.py:4244-4299). */
+int mm_upsample_nearest2d(const mm_tensor_t* x, double scale_h, double scale_w,
+                          const mm_tensor_t* y, void* stream);
+
+/* 2-D convolution, fp32, any strides for x/y/residual, weight given as a rank-4
+ * tensor [K, C/groups, R, S] with arbitrary strides (KCRS from torch, or the
+ * KRSC prepack of matrixman.prepare).  Epilogue: bias, activation, residual.
+ * Replaces conv2d_nchw and all specialised conv .entry kernels
+ * (gpumatrix.py:989-3943) and CudaBackend.convolution (cuda/backend.py:296-607). */
+int mm_conv2d(const mm_tensor_t* x, const mm_tensor_t* w, const float* bias,
+              const mm_tensor_t* residual, const mm_conv_params_t* p, const mm_tensor_t* y,
+              void* stream);
+
+/* 3xTF32 tensor-core convolution on a prepacked weight: w_hi/w_lo are
+ * [K_pad][R*S][C_pad] (C_pad % 32 == 0, K_pad % 16 == 0) with the tf32 high part
+ * and the fp32 remainder of each weight.  x/y/residual must be NHWC views
+ * (channel stride 1, C % 4 == 0).  Returns MM_ERR_UNSUPPORTED for geometries the
+ * tcgen05 path does not cover (the caller then uses mm_conv2d). */
+int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float* w_lo, int k_out, int c_in,
+                 int r, int s, int c_pad, int k_pad, const float* bias,
+                 const mm_tensor_t* residual, const mm_conv_params_t* p, const mm_tensor_t* y,
+                 void* stream);
+
+/* Split prepacked weights into the tf32 high part and the fp32 remainder
+ * (w_hi = w with its 13 low mantissa bits cleared, w_lo = w - w_hi), in place on
+ * the device: n elements of src -> hi, lo. */
+int mm_tf32_split(const float* src, float* hi, float* lo, int64_t n, void* stream);
+
+/* y[M,N] = act(alpha * x[M,K] @ w + beta * bias) with w given as a rank-2 tensor
+ * [K, N] of arbitrary strides (pass w^T of a Linear weight).  bias may be NULL
+ * or a rank-1/rank-2 broadcastable tensor.  Replaces matrix_mul (gpumatrix.py:933)
+ * and adds the OpenGL-only addmm semantics (backends/opengl/ops/matmul.py:262-281). */
+int mm_gemm(const mm_tensor_t* x, const mm_tensor_t* w, const mm_tensor_t* bias, double alpha,
+            double beta, int act, const mm_tensor_t* y, void* stream);
+
+/* YOLOv8 detect-head decode over `nlevels` feature levels.  feats[i] is an NHWC
+ * [B, H_i, W_i, 4*reg_max + nc] tensor (box logits then class logits); out is
+ * [B, 4 + nc, A] with A = sum(H_i*W_i).  Per anchor: DFL (softmax over reg_max
+ * bins, expectation with weights 0..reg_max-1), dist2bbox against the anchor
+ * centre (x+0.5, y+0.5) to xywh, times the level stride; class scores through
+ * sigmoid.  Fuses PreparedCudaDFL (preparation.py:197-268) with the decode that
+ * the reference leaves to generic ops. */
+int mm_yolo_decode(const mm_tensor_t* const* feats, const float* strides, int nlevels, int reg_max,
+                   int nc, const mm_tensor_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MATRIXMAN_B200_H */

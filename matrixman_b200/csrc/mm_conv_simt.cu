@@ -1,0 +1,369 @@
+// SIMT fp32 implicit-GEMM convolution and GEMM (exact fp32 FFMA accumulation).
+//
+// This is the general path: any strides for input/output/residual (NCHW from
+// the eager ATen route, NHWC channel slices from prepared models), any weight
+// strides (torch KCRS, prepacked KRSC, or a [K, N] GEMM operand), groups,
+// stride, padding and dilation.  The tcgen05 3xTF32 kernel (mm_conv_tc.cu)
+// takes over the NHWC shapes it supports.
+//
+// GEMM view per group g:  M = N*OH*OW output pixels, N = Kout/groups output
+// channels, K = Cg*R*S.  CTA tile BM x BN, k-step BK, each thread owns TM x TN
+// accumulators.  The next k-tile is fetched into registers while the current
+// one is consumed from shared memory.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "mm_common.cuh"
+
+namespace mm {
+
+struct ConvArgs {
+  const float* x;
+  const float* w;
+  const float* bias;
+  const float* res;
+  float* y;
+  int64_t xs[4], ws[4], ys[4], rs[4];  // strides (elements) of x, w, y, residual
+  int64_t bias_sm, bias_sn;            // bias strides along GEMM M and N
+  int n, c, h, w_in;                   // input geometry
+  int kout, oh, ow;                    // output geometry
+  int r, s, sh, sw, ph, pw, dh, dw, groups, cg, kg;
+  int act, res_before_act;
+  float alpha, beta;
+  int64_t m_total;  // n*oh*ow
+  int k_total;      // cg*r*s
+};
+
+__device__ __forceinline__ float act_apply(float v, int act) {
+  if (act == MM_ACT_RELU) return (v != v) ? v : (v > 0.f ? v : 0.f);
+  if (act == MM_ACT_SILU) return __fdiv_rn(v, 1.0f + expf(-v));
+  if (act == MM_ACT_SIGMOID) return __fdiv_rn(1.0f, 1.0f + expf(-v));
+  return v;
+}
+
+// K ordering: CFAST -> kk = (r*S + s)*Cg + c (channel fastest, NHWC-friendly),
+// else kk = (c*R + r)*S + s (tap fastest, NCHW-friendly).
+template <bool CFAST>
+__device__ __forceinline__ void decompose_k(int kk, const ConvArgs& a, int& c, int& r, int& s) {
+  if (CFAST) {
+    int rs = kk / a.cg;
+    c = kk - rs * a.cg;
+    r = rs / a.s;
+    s = rs - r * a.s;
+  } else {
+    int cr = kk / a.s;
+    s = kk - cr * a.s;
+    c = cr / a.r;
+    r = cr - c * a.r;
+  }
+}
+
+template <int BM, int BN, int BK, int TM, int TN, bool CFAST>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+    conv_simt_kernel(ConvArgs a) {
+  constexpr int NT = (BM / TM) * (BN / TN);
+  constexpr int A_PER = BM * BK / NT;
+  constexpr int B_PER = BK * BN / NT;
+  static_assert(BM * BK % NT == 0 && BK * BN % NT == 0, "tile/thread mismatch");
+  __shared__ __align__(16) float As[BK][BM + 4];
+  __shared__ __align__(16) float Bs[BK][BN + 4];
+
+  const int tid = threadIdx.x;
+  const int g = blockIdx.z;
+  const int64_t m0 = (int64_t)blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+  const int cbase = g * a.cg;
+  const int kbase = g * a.kg;
+
+  // A loader mapping.  CFAST: thread has a fixed k column and A_PER rows;
+  // otherwise a fixed row and A_PER k columns.
+  constexpr int A_ROWS_PER_PASS = CFAST ? NT / BK : 0;
+  int a_k_local = CFAST ? (tid % BK) : 0;
+  int64_t a_base[A_PER];
+  int a_ih0[A_PER], a_iw0[A_PER];
+  bool a_valid[A_PER];
+#pragma unroll
+  for (int i = 0; i < A_PER; ++i) {
+    int64_t m;
+    if (CFAST) m = m0 + tid / BK + (int64_t)i * A_ROWS_PER_PASS;
+    else m = m0 + tid % BM;
+    a_valid[i] = m < a.m_total;
+    int64_t mm_ = a_valid[i] ? m : 0;
+    int ow_ = (int)(mm_ % a.ow);
+    int64_t t = mm_ / a.ow;
+    int oh_ = (int)(t % a.oh);
+    int n_ = (int)(t / a.oh);
+    a_ih0[i] = oh_ * a.sh - a.ph;
+    a_iw0[i] = ow_ * a.sw - a.pw;
+    a_base[i] = (int64_t)n_ * a.xs[0] + (int64_t)cbase * a.xs[1];
+  }
+
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+
+  float a_reg[A_PER], b_reg[B_PER];
+
+  auto load_tile = [&](int k0) {
+    if (CFAST) {
+      int kk = k0 + a_k_local;
+      int c, r, s;
+      decompose_k<CFAST>(kk < a.k_total ? kk : 0, a, c, r, s);
+      bool kv = kk < a.k_total;
+#pragma unroll
+      for (int i = 0; i < A_PER; ++i) {
+        int ih = a_ih0[i] + r * a.dh, iw = a_iw0[i] + s * a.dw;
+        bool ok = kv && a_valid[i] && ih >= 0 && ih < a.h && iw >= 0 && iw < a.w_in;
+        a_reg[i] = ok ? __ldg(a.x + a_base[i] + (int64_t)c * a.xs[1] + (int64_t)ih * a.xs[2] +
+                              (int64_t)iw * a.xs[3])
+                      : 0.f;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < A_PER; ++i) {
+        int kk = k0 + tid / BM + i * (NT / BM);
+        int c, r, s;
+        bool kv = kk < a.k_total;
+        decompose_k<CFAST>(kv ? kk : 0, a, c, r, s);
+        int ih = a_ih0[0] + r * a.dh, iw = a_iw0[0] + s * a.dw;
+        bool ok = kv && a_valid[0] && ih >= 0 && ih < a.h && iw >= 0 && iw < a.w_in;
+        a_reg[i] = ok ? __ldg(a.x + a_base[0] + (int64_t)c * a.xs[1] + (int64_t)ih * a.xs[2] +
+                              (int64_t)iw * a.xs[3])
+                      : 0.f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < B_PER; ++i) {
+      int idx = tid + i * NT;
+      int nn = idx % BN;
+      int kk = k0 + idx / BN;
+      int kout = n0 + nn;
+      bool ok = kk < a.k_total && kout < a.kg;
+      float v = 0.f;
+      if (ok) {
+        int c, r, s;
+        decompose_k<CFAST>(kk, a, c, r, s);
+        v = __ldg(a.w + (int64_t)(kbase + kout) * a.ws[0] + (int64_t)c * a.ws[1] +
+                  (int64_t)r * a.ws[2] + (int64_t)s * a.ws[3]);
+      }
+      b_reg[i] = v;
+    }
+  };
+
+  auto store_tile = [&]() {
+#pragma unroll
+    for (int i = 0; i < A_PER; ++i) {
+      if (CFAST) As[a_k_local][tid / BK + i * A_ROWS_PER_PASS] = a_reg[i];
+      else As[tid / BM + i * (NT / BM)][tid % BM] = a_reg[i];
+    }
+#pragma unroll
+    for (int i = 0; i < B_PER; ++i) {
+      int idx = tid + i * NT;
+      Bs[idx / BN][idx % BN] = b_reg[i];
+    }
+  };
+
+  const int ty = tid / (BN / TN), tx = tid % (BN / TN);
+  load_tile(0);
+  for (int k0 = 0; k0 < a.k_total; k0 += BK) {
+    store_tile();
+    __syncthreads();
+    if (k0 + BK < a.k_total) load_tile(k0 + BK);
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float av[TM], bv[TN];
+#pragma unroll
+      for (int i = 0; i < TM; ++i) av[i] = As[kk][ty * TM + i];
+#pragma unroll
+      for (int j = 0; j < TN; ++j) bv[j] = Bs[kk][tx * TN + j];
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+
+  // Epilogue: alpha*acc + beta*bias -> act / residual -> strided store.
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    int64_t m = m0 + ty * TM + i;
+    if (m >= a.m_total) continue;
+    int ow_ = (int)(m % a.ow);
+    int64_t t = m / a.ow;
+    int oh_ = (int)(t % a.oh);
+    int n_ = (int)(t / a.oh);
+    int64_t ybase = (int64_t)n_ * a.ys[0] + (int64_t)oh_ * a.ys[2] + (int64_t)ow_ * a.ys[3];
+    int64_t rbase = (int64_t)n_ * a.rs[0] + (int64_t)oh_ * a.rs[2] + (int64_t)ow_ * a.rs[3];
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      int kout = n0 + tx * TN + j;
+      if (kout >= a.kg) continue;
+      int kk = kbase + kout;
+      float v = acc[i][j] * a.alpha;
+      if (a.bias) v += a.beta * a.bias[m * a.bias_sm + (int64_t)kk * a.bias_sn];
+      if (a.res && a.res_before_act) v += a.res[rbase + (int64_t)kk * a.rs[1]];
+      v = act_apply(v, a.act);
+      if (a.res && !a.res_before_act) v += a.res[rbase + (int64_t)kk * a.rs[1]];
+      a.y[ybase + (int64_t)kk * a.ys[1]] = v;
+    }
+  }
+}
+
+template <int BM, int BN, int BK, int TM, int TN>
+static int launch_conv(const ConvArgs& a, bool cfast, cudaStream_t s) {
+  int64_t mt = (a.m_total + BM - 1) / BM;
+  if (mt > 0x7fffffffLL) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d: too many output pixels");
+  dim3 grid((unsigned)mt, (unsigned)((a.kg + BN - 1) / BN), (unsigned)a.groups);
+  if (grid.y > 65535 || grid.z > 65535) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d: grid too large");
+  constexpr int NT = (BM / TM) * (BN / TN);
+  if (cfast) conv_simt_kernel<BM, BN, BK, TM, TN, true><<<grid, NT, 0, s>>>(a);
+  else conv_simt_kernel<BM, BN, BK, TM, TN, false><<<grid, NT, 0, s>>>(a);
+  MM_LAUNCH_CHECK("mm_conv2d launch");
+  return MM_OK;
+}
+
+int conv_simt_dispatch(const ConvArgs& a, bool cfast, cudaStream_t s) {
+  if (a.kg <= 16) return launch_conv<128, 16, 16, 8, 2>(a, cfast, s);   // 128 threads
+  if (a.kg <= 32) return launch_conv<128, 32, 16, 8, 4>(a, cfast, s);   // 128 threads
+  if (a.m_total <= 4096) return launch_conv<64, 64, 16, 4, 4>(a, cfast, s);  // 256 threads
+  return launch_conv<128, 64, 16, 8, 4>(a, cfast, s);                    // 256 threads
+}
+
+}  // namespace mm
+
+using namespace mm;
+
+extern "C" int mm_conv2d(const mm_tensor_t* x, const mm_tensor_t* w, const float* bias,
+                         const mm_tensor_t* residual, const mm_conv_params_t* p,
+                         const mm_tensor_t* y, void* stream) {
+  int rc;
+  if ((rc = validate(x, "mm_conv2d input", MM_F32)) != MM_OK) return rc;
+  if ((rc = validate(w, "mm_conv2d weight", MM_F32)) != MM_OK) return rc;
+  if ((rc = validate(y, "mm_conv2d output", MM_F32)) != MM_OK) return rc;
+  if (p == nullptr) return fail(MM_ERR_INVALID, "mm_conv2d: null params");
+  if (x->ndim != 4 || w->ndim != 4 || y->ndim != 4)
+    return fail(MM_ERR_UNSUPPORTED, "mm_conv2d: only rank-4 NCHW-logical tensors are supported");
+  if (residual && (rc = validate(residual, "mm_conv2d residual", MM_F32)) != MM_OK) return rc;
+  ConvArgs a{};
+  a.x = (const float*)x->data;
+  a.w = (const float*)w->data;
+  a.bias = bias;
+  a.res = residual ? (const float*)residual->data : nullptr;
+  a.y = (float*)y->data;
+  for (int i = 0; i < 4; ++i) {
+    a.xs[i] = x->stride[i];
+    a.ws[i] = w->stride[i];
+    a.ys[i] = y->stride[i];
+    a.rs[i] = residual ? residual->stride[i] : 0;
+  }
+  a.bias_sm = 0;
+  a.bias_sn = 1;
+  a.n = (int)x->size[0];
+  a.c = (int)x->size[1];
+  a.h = (int)x->size[2];
+  a.w_in = (int)x->size[3];
+  a.kout = (int)w->size[0];
+  a.r = (int)w->size[2];
+  a.s = (int)w->size[3];
+  a.sh = p->stride_h;
+  a.sw = p->stride_w;
+  a.ph = p->pad_h;
+  a.pw = p->pad_w;
+  a.dh = p->dil_h;
+  a.dw = p->dil_w;
+  a.groups = p->groups;
+  a.act = p->act;
+  a.res_before_act = p->residual_before_act;
+  a.alpha = 1.f;
+  a.beta = 1.f;
+  if (a.groups <= 0 || a.c % a.groups || a.kout % a.groups || w->size[1] != a.c / a.groups)
+    return fail(MM_ERR_UNSUPPORTED,
+                "mm_conv2d: groups/weight channels are unsupported (expected weight C == input C / groups)");
+  if (a.sh <= 0 || a.sw <= 0 || a.dh <= 0 || a.dw <= 0 || a.ph < 0 || a.pw < 0)
+    return fail(MM_ERR_UNSUPPORTED, "mm_conv2d: invalid stride, padding, or dilation");
+  a.cg = a.c / a.groups;
+  a.kg = a.kout / a.groups;
+  int64_t oh = ((int64_t)a.h + 2 * a.ph - (int64_t)a.dh * (a.r - 1) - 1) / a.sh + 1;
+  int64_t ow = ((int64_t)a.w_in + 2 * a.pw - (int64_t)a.dw * (a.s - 1) - 1) / a.sw + 1;
+  if (oh <= 0 || ow <= 0) return fail(MM_ERR_INVALID, "mm_conv2d: output dimensions must be positive");
+  if (y->size[0] != a.n || y->size[1] != a.kout || y->size[2] != oh || y->size[3] != ow)
+    return fail(MM_ERR_INVALID, "mm_conv2d: output shape mismatch");
+  if (residual) {
+    for (int i = 0; i < 4; ++i)
+      if (residual->size[i] != y->size[i]) return fail(MM_ERR_INVALID, "mm_conv2d: residual shape mismatch");
+  }
+  a.oh = (int)oh;
+  a.ow = (int)ow;
+  a.m_total = (int64_t)a.n * oh * ow;
+  int64_t kt = (int64_t)a.cg * a.r * a.s;
+  if (kt > 0x7fffffff) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d: reduction too large");
+  a.k_total = (int)kt;
+  if (a.m_total == 0 || a.kout == 0) return MM_OK;
+  // Channel-fastest K order when channels are the densest input dim (NHWC).
+  bool cfast = x->stride[1] == 1 && a.c > 1;
+  return conv_simt_dispatch(a, cfast, resolve_stream(stream));
+}
+
+extern "C" int mm_gemm(const mm_tensor_t* x, const mm_tensor_t* w, const mm_tensor_t* bias,
+                       double alpha, double beta, int act, const mm_tensor_t* y, void* stream) {
+  int rc;
+  if ((rc = validate(x, "mm_gemm lhs", MM_F32)) != MM_OK) return rc;
+  if ((rc = validate(w, "mm_gemm rhs", MM_F32)) != MM_OK) return rc;
+  if ((rc = validate(y, "mm_gemm output", MM_F32)) != MM_OK) return rc;
+  if (x->ndim != 2 || w->ndim != 2 || y->ndim != 2)
+    return fail(MM_ERR_UNSUPPORTED, "mm_gemm: rank-2 operands required");
+  int64_t m = x->size[0], k = x->size[1], n = w->size[1];
+  if (w->size[0] != k)
+    return fail(MM_ERR_INVALID, "mm_gemm: shapes cannot be multiplied (" + std::to_string(m) + "x" +
+                                    std::to_string(k) + " and " + std::to_string(w->size[0]) + "x" +
+                                    std::to_string(n) + ")");
+  if (y->size[0] != m || y->size[1] != n) return fail(MM_ERR_INVALID, "mm_gemm: output shape mismatch");
+  if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+    return fail(MM_ERR_UNSUPPORTED, "mm_gemm: dimension too large");
+  ConvArgs a{};
+  a.x = (const float*)x->data;
+  a.w = (const float*)w->data;
+  a.y = (float*)y->data;
+  a.res = nullptr;
+  // x as [M, K, 1, 1]; w as conv weight [N, K, 1, 1]; y as [M, N, 1, 1].
+  a.xs[0] = x->stride[0]; a.xs[1] = x->stride[1]; a.xs[2] = 0; a.xs[3] = 0;
+  a.ws[0] = w->stride[1]; a.ws[1] = w->stride[0]; a.ws[2] = 0; a.ws[3] = 0;
+  a.ys[0] = y->stride[0]; a.ys[1] = y->stride[1]; a.ys[2] = 0; a.ys[3] = 0;
+  if (bias) {
+    if ((rc = validate(bias, "mm_gemm bias", MM_F32)) != MM_OK) return rc;
+    if (bias->ndim == 1) {
+      if (bias->size[0] != n && bias->size[0] != 1) return fail(MM_ERR_INVALID, "mm_gemm: bias shape");
+      a.bias_sm = 0;
+      a.bias_sn = bias->size[0] == 1 ? 0 : bias->stride[0];
+    } else if (bias->ndim == 2) {
+      if ((bias->size[0] != m && bias->size[0] != 1) || (bias->size[1] != n && bias->size[1] != 1))
+        return fail(MM_ERR_INVALID, "mm_gemm: bias shape");
+      a.bias_sm = bias->size[0] == 1 ? 0 : bias->stride[0];
+      a.bias_sn = bias->size[1] == 1 ? 0 : bias->stride[1];
+    } else {
+      return fail(MM_ERR_UNSUPPORTED, "mm_gemm: bias rank must be 1 or 2");
+    }
+    a.bias = (const float*)bias->data;
+  }
+  a.n = (int)m; a.c = (int)k; a.h = 1; a.w_in = 1;
+  a.kout = (int)n; a.oh = 1; a.ow = 1;
+  a.r = 1; a.s = 1; a.sh = 1; a.sw = 1; a.ph = 0; a.pw = 0; a.dh = 1; a.dw = 1;
+  a.groups = 1; a.cg = (int)k; a.kg = (int)n;
+  a.act = act;
+  a.res_before_act = 0;
+  a.alpha = (float)alpha;
+  a.beta = (float)beta;
+  a.m_total = m;
+  a.k_total = (int)k;
+  if (m == 0 || n == 0) return MM_OK;
+  if (k == 0) {
+    // alpha*0 + beta*bias
+    if (!bias) return mm_fill(y, 0.0, stream);
+  }
+  return conv_simt_dispatch(a, x->stride[1] == 1, resolve_stream(stream));
+}

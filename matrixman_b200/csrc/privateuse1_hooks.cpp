@@ -1,0 +1,140 @@
+// C++ PrivateUse1 plumbing for the `matrixman` device, built as a small torch
+// extension (torch.utils.cpp_extension) in-tree.
+//
+// Replaces drivers/matrixman/native/autograd_privateuse1.cpp of the reference
+// (lines 7-66), whose hooks and DeviceGuard hard-wired one device and a no-op
+// default stream.  Here the guard reports the real CUDA device count, switches
+// the current CUDA device, and maps the c10 default stream of each device onto
+// the runtime stream of libmatrixman_b200 (queried / synchronised through the
+// C ABI).  The library is resolved at run time with dlsym, so this extension
+// links against neither CUDA nor libmatrixman_b200 directly.
+#include <ATen/detail/PrivateUse1HooksInterface.h>
+#include <c10/core/impl/DeviceGuardImplInterface.h>
+#include <dlfcn.h>
+#include <torch/extension.h>
+
+#include <atomic>
+
+namespace {
+
+using count_fn = int (*)(int*);
+using dev_fn = int (*)(int);
+using stream_fn = int (*)(int, void**);
+using sync_fn = int (*)(void*, int64_t);
+using query_fn = int (*)(void*, int*);
+
+template <class F>
+F resolve(const char* name) {
+  void* p = dlsym(RTLD_DEFAULT, name);
+  TORCH_CHECK(p != nullptr, "matrixman hooks: libmatrixman_b200 symbol ", name,
+              " not loaded (import matrixman_b200 first)");
+  return reinterpret_cast<F>(p);
+}
+
+thread_local int t_current_device = 0;
+
+int device_count() {
+  int n = 0;
+  if (resolve<count_fn>("mm_device_count")(&n) != 0) return 0;
+  return n;
+}
+
+void* runtime_stream(int device) {
+  void* s = nullptr;
+  resolve<dev_fn>("mm_init")(device);
+  resolve<stream_fn>("mm_runtime_stream")(device, &s);
+  return s;
+}
+
+class MatrixManHooks final : public at::PrivateUse1HooksInterface {
+ public:
+  bool isBuilt() const override { return true; }
+  bool isAvailable() const override { return device_count() > 0; }
+  bool hasPrimaryContext(c10::DeviceIndex) const override { return true; }
+  c10::Device getDeviceFromPtr(void*) const override {
+    return c10::Device(c10::DeviceType::PrivateUse1, (c10::DeviceIndex)t_current_device);
+  }
+};
+
+class MatrixManGuardImpl final : public c10::impl::DeviceGuardImplInterface {
+ public:
+  c10::DeviceType type() const override { return c10::DeviceType::PrivateUse1; }
+
+  c10::Device exchangeDevice(c10::Device d) const override {
+    c10::Device old = getDevice();
+    if (d.index() != old.index()) setDevice(d);
+    return old;
+  }
+
+  c10::Device getDevice() const override {
+    return c10::Device(c10::DeviceType::PrivateUse1, (c10::DeviceIndex)t_current_device);
+  }
+
+  void setDevice(c10::Device d) const override {
+    TORCH_CHECK(d.type() == c10::DeviceType::PrivateUse1, "matrixman guard: wrong device type");
+    int idx = d.index() < 0 ? 0 : d.index();
+    TORCH_CHECK(resolve<dev_fn>("mm_set_device")(idx) == 0, "matrixman guard: cannot select device ", idx);
+    t_current_device = idx;
+  }
+
+  void uncheckedSetDevice(c10::Device d) const noexcept override {
+    int idx = d.index() < 0 ? 0 : d.index();
+    void* p = dlsym(RTLD_DEFAULT, "mm_set_device");
+    if (p) reinterpret_cast<dev_fn>(p)(idx);
+    t_current_device = idx;
+  }
+
+  // One runtime stream per device (id 0 == the libmatrixman_b200 runtime stream).
+  c10::Stream getStream(c10::Device d) const override {
+    return c10::Stream(c10::Stream::DEFAULT, d);
+  }
+  c10::Stream getNewStream(c10::Device d, int) const override {
+    return c10::Stream(c10::Stream::DEFAULT, d);
+  }
+  c10::Stream exchangeStream(c10::Stream s) const noexcept override { return s; }
+
+  c10::DeviceIndex deviceCount() const noexcept override {
+    void* p = dlsym(RTLD_DEFAULT, "mm_device_count");
+    if (!p) return 0;
+    int n = 0;
+    if (reinterpret_cast<count_fn>(p)(&n) != 0) return 0;
+    return (c10::DeviceIndex)n;
+  }
+
+  bool queryStream(const c10::Stream& s) const override {
+    int done = 1;
+    resolve<query_fn>("mm_stream_query")(runtime_stream(s.device_index()), &done);
+    return done != 0;
+  }
+
+  void synchronizeStream(const c10::Stream& s) const override {
+    TORCH_CHECK(resolve<sync_fn>("mm_stream_sync")(runtime_stream(s.device_index()), -1) == 0,
+                "matrixman guard: stream synchronize failed");
+  }
+
+  void synchronizeDevice(const c10::DeviceIndex idx) const override {
+    TORCH_CHECK(resolve<sync_fn>("mm_stream_sync")(runtime_stream(idx), -1) == 0,
+                "matrixman guard: device synchronize failed");
+  }
+};
+
+C10_REGISTER_GUARD_IMPL(PrivateUse1, MatrixManGuardImpl);
+
+MatrixManHooks g_hooks;
+std::atomic<bool> g_registered{false};
+
+void register_hooks() {
+  bool expected = false;
+  if (g_registered.compare_exchange_strong(expected, true)) {
+    at::RegisterPrivateUse1HooksInterface(&g_hooks);
+  }
+}
+
+int guard_device_count() { return (int)MatrixManGuardImpl().deviceCount(); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("register_hooks", &register_hooks, "Register the matrixman PrivateUse1 hooks");
+  m.def("device_count", &guard_device_count, "Device count seen by the DeviceGuard");
+}

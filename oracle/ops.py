@@ -1,0 +1,158 @@
+"""Per-op CPU restatement (torch CPU fp32 / NumPy) -- test infrastructure only.
+
+Each function states the semantics of one op on MatrixMan's tensor path and
+cites the reference implementation it follows.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+
+def conv2d(x, w, b=None, stride=1, padding=0, dilation=1, groups=1):
+    """NCHW direct convolution (reference generic kernel conv2d_nchw,
+    backends/cuda/gpumatrix.py:989; checked against torch in
+    diagnostics/matrixman_conv_demo.py:57-70)."""
+    return F.conv2d(x, w, b, stride, padding, dilation, groups)
+
+
+def conv2d_loops(x: np.ndarray, w: np.ndarray, b=None, stride=(1, 1), padding=(0, 0),
+                 dilation=(1, 1), groups=1) -> np.ndarray:
+    """Loop-nest convolution with the index rule of reference_conv2d
+    (backends/cuda/conv2d.py:13-46); float64 accumulation.  Small cases only."""
+    n, c, h, wd = x.shape
+    k, cg, r, s = w.shape
+    oh = (h + 2 * padding[0] - dilation[0] * (r - 1) - 1) // stride[0] + 1
+    ow = (wd + 2 * padding[1] - dilation[1] * (s - 1) - 1) // stride[1] + 1
+    out = np.zeros((n, k, oh, ow), dtype=np.float64)
+    kg = k // groups
+    for bi in range(n):
+        for ko in range(k):
+            g = ko // kg
+            for oy in range(oh):
+                for ox in range(ow):
+                    acc = 0.0 if b is None else float(b[ko])
+                    for ci in range(cg):
+                        for ky in range(r):
+                            iy = oy * stride[0] - padding[0] + ky * dilation[0]
+                            if iy < 0 or iy >= h:
+                                continue
+                            for kx in range(s):
+                                ix = ox * stride[1] - padding[1] + kx * dilation[1]
+                                if 0 <= ix < wd:
+                                    acc += float(x[bi, g * cg + ci, iy, ix]) * float(w[ko, ci, ky, kx])
+                    out[bi, ko, oy, ox] = acc
+    return out.astype(np.float32)
+
+
+def batch_norm_eval(x, mean, var, weight, bias, eps=1e-5):
+    """Eval BatchNorm ((x-mean)/sqrt(var+eps)*w+b), batch_norm_inference
+    (backends/cuda/gpumatrix.py:3945-4010), known answer in
+    backends/cuda/batch_norm.py:9-22."""
+    return F.batch_norm(x, mean, var, weight, bias, False, 0.0, eps)
+
+
+def silu(x):
+    """x * sigmoid(x) (backends/cuda/gpumatrix.py:4012; backends/cuda/silu.py:9-11)."""
+    return F.silu(x)
+
+
+def sigmoid(x):
+    """1 / (1 + exp(-x)) (backends/cuda/gpumatrix.py:581)."""
+    return torch.sigmoid(x)
+
+
+def relu(x):
+    """max(x, 0) with NaN passthrough (OpenGL-only in the reference:
+    backends/opengl/ops/activation.py:278-306, 334-393)."""
+    return F.relu(x)
+
+
+def softmax(x, dim):
+    """Stable softmax along dim (matrix_softmax, backends/cuda/gpumatrix.py:784-931)."""
+    return torch.softmax(x, dim)
+
+
+def softmax_exact(x: torch.Tensor, dim: int) -> torch.Tensor:
+    """Correctly rounded fp32 softmax computed in float64 (the exact reference
+    against which ulp distances are measured)."""
+    xd = x.double()
+    e = torch.exp(xd - xd.amax(dim, keepdim=True))
+    return (e / e.sum(dim, keepdim=True)).float()
+
+
+def log_softmax(x, dim):
+    return torch.log_softmax(x, dim)
+
+
+def max_pool2d(x, kernel, stride=None, padding=0, dilation=1, ceil_mode=False):
+    """Max pooling with -inf padding (max_pool2d_5x5_s1_p2,
+    backends/cuda/gpumatrix.py:74-169 for 5x5; generic window semantics of
+    backends/opengl/ops/pooling.py:47-69 and 105-190)."""
+    return F.max_pool2d(x, kernel, stride, padding, dilation, ceil_mode)
+
+
+def sppf_chain(x):
+    """Three chained 5x5/s1/p2 max pools (the SPPF block)."""
+    y1 = F.max_pool2d(x, 5, 1, 2)
+    y2 = F.max_pool2d(y1, 5, 1, 2)
+    y3 = F.max_pool2d(y2, 5, 1, 2)
+    return y1, y2, y3
+
+
+def avg_pool2d(x, kernel, stride=None, padding=0, ceil_mode=False, count_include_pad=True,
+               divisor_override=None):
+    return F.avg_pool2d(x, kernel, stride, padding, ceil_mode, count_include_pad, divisor_override)
+
+
+def adaptive_avg_pool2d(x, size):
+    return F.adaptive_avg_pool2d(x, size)
+
+
+def mean(x, dims, keepdim=False):
+    """mean over dims (backends/opengl/ops/reduction.py:136-221)."""
+    return x.mean(dims, keepdim=keepdim)
+
+
+def upsample_nearest(x, size=None, scale_factor=None):
+    """Nearest upsampling.  For integer output sizes the reference's index rule
+    is y = oy*H//Ho (backends/cuda/upsample.py:9-14); torch's rule with the
+    size ratio agrees on integer scale factors."""
+    return F.interpolate(x, size=size, scale_factor=scale_factor, mode="nearest")
+
+
+def nearest_reference(values: np.ndarray, oh: int, ow: int) -> np.ndarray:
+    """Integer nearest index rule of backends/cuda/upsample.py:9-14."""
+    ih, iw = values.shape[-2:]
+    ys = (np.arange(oh) * ih // oh).astype(np.int64)
+    xs = (np.arange(ow) * iw // ow).astype(np.int64)
+    return values[:, :, ys[:, None], xs[None, :]]
+
+
+def addmm(bias, a, b, beta=1.0, alpha=1.0):
+    """beta*bias + alpha*(a @ b) (backends/opengl/ops/matmul.py:262-281)."""
+    return torch.addmm(bias, a, b, beta=beta, alpha=alpha)
+
+
+def fold_conv_bn(w, b, mean, var, gamma, beta, eps):
+    """BN folding of preparation.py:385-392: scale = gamma/sqrt(var+eps),
+    W' = W*scale, b' = (b - mean)*scale + beta."""
+    scale = gamma / torch.sqrt(var + eps)
+    return w * scale.reshape(-1, 1, 1, 1), (b - mean) * scale + beta
+
+
+def yolo_decode(feats, strides, reg_max=16, nc=80):
+    """DFL + dist2bbox + sigmoid of the YOLOv8 head over per-level
+    [B, 4*reg_max+nc, H, W] features (PreparedCudaDFL chain,
+    preparation.py:222-268, followed by the anchor decode)."""
+    from workloads.yolov8 import DFL, dist2bbox, make_anchors
+    b = feats[0].shape[0]
+    no = 4 * reg_max + nc
+    flat = torch.cat([f.reshape(b, no, -1) for f in feats], 2)
+    anchors, stride_t = make_anchors(feats, strides)
+    box, cls = flat.split((4 * reg_max, nc), 1)
+    dfl = DFL(reg_max)
+    dbox = dist2bbox(dfl(box), anchors.transpose(0, 1).unsqueeze(0), dim=1) * stride_t.transpose(0, 1)
+    return torch.cat((dbox, cls.sigmoid()), 1)
