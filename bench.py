@@ -1,0 +1,350 @@
+"""Benchmark: YOLOv8n-architecture fp32 640x640 inference images/s on B200.
+
+One step = one prepared YOLOv8n forward over a batch of 64 synthetic
+640x640 images per GPU (weak scaling: every rank runs a whole-model replica
+on its own batch slice).  ``value`` is measured with inputs resident in HBM;
+``e2e`` repeats the same metric through the public API from pinned host
+buffers (upload, forward, ``.cpu()`` of the [B, 84, 8400] result).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Under torchrun every rank runs; timing is on the device (CUDA events on the
+runtime stream) with a barrier + synchronize on both sides, max over ranks.
+``--impl reference`` times the reference's ground-truth implementation of the
+path (stock PyTorch CPU fp32 running the same unprepared model) on the host
+cores of rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "YOLOv8n 640x640 fp32 images/sec"
+UNIT = "images/s"
+BATCH = 64
+IMAGE = 640
+NC = 80
+ANCHORS = (IMAGE // 8) ** 2 + (IMAGE // 16) ** 2 + (IMAGE // 32) ** 2
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--batch", type=int, default=BATCH)
+    p.add_argument("--e2e-steps", type=int, default=None)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="mm_clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        sm = []
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+            except ValueError:
+                pass
+            for name, flag in zip(names, r[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        smax = None
+        try:
+            smax = float(rows[0][2])
+        except ValueError:
+            pass
+        load = [s for s in sm if smax and s > 0.3 * smax] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def profile_launches(matrixman, prepared, x_dev) -> dict:
+    """One eager forward with CUDA events around every native launch."""
+    from matrixman_b200 import profiling
+    cfg = matrixman.config
+    old_graphs, old_timing = cfg.cudaGraphs, cfg.gpuTiming
+    cfg.cuda_graphs = False
+    cfg.gpu_timing = True
+    profiling.launch_times.records.clear()
+    try:
+        import torch
+        with torch.no_grad():
+            prepared(x_dev)
+        summary = profiling.launch_times.summary()
+    finally:
+        cfg.cuda_graphs = old_graphs
+        cfg.gpu_timing = old_timing
+    return summary
+
+
+def cpu_baseline(model, batch_sample: int, min_seconds: float = 12.0) -> dict:
+    """Stock PyTorch CPU fp32 on this host's cores (the reference's ground truth)."""
+    import torch
+    import workloads as W
+    from oracle.models import cpu_model_name
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x = W.yolo_input(batch_sample, seed=99)
+    with torch.no_grad():
+        model(x)  # warm-up
+        n, t0 = 0, time.perf_counter()
+        while True:
+            model(x)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= min_seconds or n >= 50:
+                break
+    return {"value": n * batch_sample / el, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} forwards of an unprepared YOLOv8n bs{batch_sample} 640x640 on torch CPU "
+                      f"fp32 ({cpu_model_name()}, {threads} threads), {el:.1f} s"}
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    import matrixman_b200 as matrixman
+    import workloads as W
+    from matrixman_b200 import profiling, runtime
+    from workloads.yolov8 import macs_per_image
+
+    world, rank, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    runtime.set_device(local)
+    matrixman.init()
+    rt = runtime.get_runtime(local)
+    batch = args.batch
+    model = W.yolov8_model("n")
+    prepared = matrixman.prepare(model)
+    x_host = W.yolo_input(batch, seed=1000 + rank)
+    x_dev = matrixman.to_device(x_host, device=local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        rt.synchronize()
+
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 3)):
+            y = prepared(x_dev)
+        del y
+        barrier()
+        clocks = ClockSampler(local)
+        clocks.start()
+        timer = runtime.Timer(rt)
+        launches0 = profiling.total_launches()
+        barrier()
+        timer.start()
+        for _ in range(args.steps):
+            y = prepared(x_dev)
+        timer.stop()
+        ms_total = timer.elapsed_ms()
+        launch_calls = profiling.total_launches() - launches0
+        barrier()
+        clock_info = clocks.stop()
+    ms_step = ms_total / args.steps
+    if world > 1:
+        t = torch.tensor([ms_step], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = float(t.item())
+    value = world * batch / (ms_step / 1e3)
+
+    # End to end: pinned host input -> public API -> .cpu() of the result.
+    e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+    x_pinned = x_host.pin_memory() if torch.cuda.is_available() else x_host
+    with torch.no_grad():
+        for _ in range(2):
+            prepared(matrixman.to_device(x_pinned, device=local)).cpu()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            out = prepared(matrixman.to_device(x_pinned, device=local)).cpu()
+        barrier()
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": world * batch / e2e_s, "unit": UNIT,
+           "h2d_bytes_per_step": int(x_host.numel() * 4),
+           "d2h_bytes_per_step": int(out.numel() * 4), "ms_per_step": e2e_s * 1e3}
+    return {"world": world, "rank": rank, "local": local, "value": value, "ms_step": ms_step,
+            "clocks": clock_info, "e2e": e2e, "launch_calls": launch_calls, "prepared": prepared,
+            "x_dev": x_dev, "model": model, "macs": macs_per_image(model), "batch": batch,
+            "matrixman": matrixman, "dist": dist if world > 1 else None}
+
+
+CONV_ENTRIES = ("mm_conv2d", "mm_conv2d_tc")
+
+
+def roofline(res: dict) -> tuple[dict, int, dict]:
+    """Dominant kernel family (convolution) from one event-timed eager forward.
+
+    achieved = algorithmic conv FLOPs of one forward (2 * MACs * batch) / the
+    summed device time of the conv launches.  The tensor roofline of the
+    3xTF32 split is one third of the dense TF32 rate, which is half of the
+    measured dense bf16 rate.
+    """
+    peaks = measured_peaks()
+    summary = profile_launches(res["matrixman"], res["prepared"], res["x_dev"])
+    total_ms = sum(v["ms"] for v in summary.values()) or 1e-9
+    conv_ms = sum(summary[k]["ms"] for k in CONV_ENTRIES if k in summary)
+    conv_launches = sum(summary[k]["launches"] for k in CONV_ENTRIES if k in summary)
+    flops = 2.0 * res["macs"] * res["batch"]
+    achieved = flops / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
+    peak = peaks["bf16_tflops"] / 2.0 / 3.0
+    kernels_per_forward = sum(v["launches"] for v in summary.values())
+    roof = {"bound": "tensor", "kernel": "+".join(k for k in CONV_ENTRIES if k in summary),
+            "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4) if peak else None, "traffic": None,
+            "peak_basis": f"{peaks['source']} bf16 {peaks['bf16_tflops']} TF/s / 2 (tf32) / 3 (3xTF32 split)",
+            "launches_per_forward": conv_launches, "share_of_forward": round(conv_ms / total_ms, 3),
+            "forward_ms_eager_events": round(total_ms, 3)}
+    shares = {k: {"launches": v["launches"], "ms": round(v["ms"], 4), "share": round(v["ms"] / total_ms, 4)}
+              for k, v in sorted(summary.items(), key=lambda kv: -kv[1]["ms"])}
+    return roof, kernels_per_forward, shares
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+    res = run_b200(args)
+    roof, kernels_per_forward, shares = roofline(res)
+    line = {
+        "metric": METRIC, "value": round(res["value"], 2), "unit": UNIT, "n_gpus": res["world"],
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(res["ms_step"], 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic U[0,1] images, random-init weights (seeded)",
+        "config": {"workload": f"yolov8n 640x640 fp32 inference, {res['batch']} images per GPU, "
+                               "prepared (BN folded, NHWC, CUDA graph)",
+                   "batch_per_gpu": res["batch"], "global_batch": res["batch"] * res["world"],
+                   "image": [IMAGE, IMAGE], "parallelism": f"replicas{res['world']}",
+                   "l2": "inputs larger than L2 (315 MB input per step per GPU)"},
+        "e2e": res["e2e"], "roofline": roof,
+        "gpu_launches": kernels_per_forward * args.steps, "clocks": res["clocks"],
+        "kernel_shares": shares,
+    }
+    if res["world"] == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(res["model"], 8)
+    if res["dist"] is not None:
+        res["dist"].barrier()
+        res["dist"].destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the path's CPU ground truth (unprepared model, torch CPU fp32)."""
+    if rank != 0:
+        return
+    import torch
+    import workloads as W
+    from oracle.models import cpu_model_name
+    model = W.yolov8_model("n")
+    sample = 8
+    x = W.yolo_input(sample, seed=99)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    steps = max(1, min(args.steps, 5))
+    with torch.no_grad():
+        for _ in range(max(1, min(args.warmup, 1))):
+            model(x)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            model(x)
+        el = time.perf_counter() - t0
+    value = steps * sample / el
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": 1, "ms_per_step": round(el / steps * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+        "data": "synthetic U[0,1] images, random-init weights (seeded)",
+        "config": {"workload": "yolov8n 640x640 fp32 inference (unprepared, torch CPU fp32), "
+                               f"bounded sample of {sample} images per step",
+                   "batch_per_gpu": BATCH, "image": [IMAGE, IMAGE], "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{steps} x bs{sample} forwards on {cpu_model_name()}"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

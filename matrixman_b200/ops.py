@@ -78,9 +78,12 @@ def empty_like(t: MatrixManTensor, shape=None) -> MatrixManTensor:
 
 def _launch(name: str, *args) -> None:
     lib = _lib_handle()
+    token = profiling.launch_times.begin(name, args[-1]) if profiling.gpu_timing_enabled() else None
     status = getattr(lib, name)(*args)
     if status != _lib.MM_OK:
         _lib.check(status, name)
+    if token is not None:
+        profiling.launch_times.end(token)
     profiling.count_launch(name)
     if config.cudaDisableAsyncQueue or config.cudaDebug:
         get_runtime().synchronize()

@@ -45,10 +45,62 @@ def dispatch_scope(op: str):
         dispatch_calls[op] += 1
 
 
+class LaunchTimes:
+    """CUDA-event bracket around every native launch on its own stream
+    (enabled by ``config.gpu_timing``; eager execution only -- a captured
+    graph has no host-side launches to bracket)."""
+
+    def __init__(self):
+        self.records: list[tuple[str, object, object, object]] = []
+
+    def begin(self, name: str, stream) -> object:
+        import ctypes
+        from . import _lib
+        lib = _lib.load()
+        e0, e1 = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(lib.mm_event_create(ctypes.byref(e0), 1), "event create")
+        _lib.check(lib.mm_event_create(ctypes.byref(e1), 1), "event create")
+        _lib.check(lib.mm_event_record(e0, stream), "event record")
+        return (name, e0, e1, stream)
+
+    def end(self, token) -> None:
+        from . import _lib
+        lib = _lib.load()
+        _lib.check(lib.mm_event_record(token[2], token[3]), "event record")
+        self.records.append(token)
+
+    def summary(self) -> dict:
+        """{entry point: {"launches": n, "ms": total}} (synchronises)."""
+        import ctypes
+        from . import _lib
+        lib = _lib.load()
+        out: dict = {}
+        for name, e0, e1, _s in self.records:
+            _lib.check(lib.mm_event_sync(e1, config.waitTimeoutMs), "event sync")
+            ms = ctypes.c_float()
+            _lib.check(lib.mm_event_elapsed_ms(e0, e1, ctypes.byref(ms)), "event elapsed")
+            rec = out.setdefault(name, {"launches": 0, "ms": 0.0, "each_ms": []})
+            rec["launches"] += 1
+            rec["ms"] += float(ms.value)
+            rec["each_ms"].append(float(ms.value))
+            lib.mm_event_destroy(e0)
+            lib.mm_event_destroy(e1)
+        self.records.clear()
+        return out
+
+
+launch_times = LaunchTimes()
+
+
+def gpu_timing_enabled() -> bool:
+    return bool(config._values["gpuTiming"])
+
+
 def reset() -> None:
     launches.clear()
     dispatch_seconds.clear()
     dispatch_calls.clear()
+    launch_times.records.clear()
 
 
 def report(frame_count: int | None = None) -> str:

@@ -1,0 +1,77 @@
+"""Whole-model parity on the device against the unprepared CPU fp32 oracle
+(max relative error <= 1e-4, the reference's relative_max measure)."""
+
+import pytest
+import torch
+
+import workloads as W
+from oracle.models import run_cpu
+from oracle.tolerance import CONV_GEMM_REL, max_rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(mm, model, x, prepared=True, calls=3):
+    ref = run_cpu(model, x)
+    target = mm.prepare(model) if prepared else model
+    with torch.no_grad():
+        for _ in range(calls):  # eager warm-up, graph capture, replay
+            y = target(mm.to_device(x)).cpu()
+            err = max_rel_err(y, ref)
+            assert err < CONV_GEMM_REL, f"max relative error {err:.3g}"
+    return target
+
+
+def test_mlp_bs256(mm):
+    model = W.mlp_model()
+    x = W.mlp_input(256)
+    _check(mm, model, x, prepared=False, calls=1)
+    p = _check(mm, model, x)
+    rep = p._matrixman_preparation_report
+    assert rep.linear_units_prepared == 3
+
+
+def test_resnet18_bs32(mm):
+    model = W.resnet18_model()
+    x = W.resnet18_input(32)
+    p = _check(mm, model, x)
+    rep = p._matrixman_preparation_report
+    assert rep.folded == 20 and rep.remaining_batch_norm_modules == 0
+    assert rep.block_units_prepared["BasicBlock"] == 8
+
+
+def test_resnet18_unprepared_eager(mm):
+    model = W.resnet18_model()
+    x = W.resnet18_input(2, size=96)
+    _check(mm, model, x, prepared=False, calls=1)
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_yolov8n_prepared(mm, batch):
+    model = W.yolov8_model("n")
+    x = W.yolo_input(batch)
+    p = _check(mm, model, x)
+    rep = p._matrixman_preparation_report
+    assert rep.folded == 57 and rep.detection_head_prepared == 1
+
+
+def test_yolov8n_unprepared_eager(mm):
+    model = W.yolov8_model("n")
+    x = W.yolo_input(1, size=320)
+    _check(mm, model, x, prepared=False, calls=1)
+
+
+def test_yolov8m_prepared_bs1(mm):
+    model = W.yolov8_model("m")
+    x = W.yolo_input(1)
+    _check(mm, model, x, calls=2)
+
+
+def test_auto_prepare_lazy(mm):
+    model = W.yolov8_model("n")
+    lazy = mm.auto_prepare(model)
+    x = W.yolo_input(1, size=320)
+    ref = run_cpu(model, x)
+    with torch.no_grad():
+        y = lazy(mm.to_device(x)).cpu()
+    assert max_rel_err(y, ref) < CONV_GEMM_REL
