@@ -130,7 +130,7 @@ def measured_peaks() -> dict:
 
 def profile_launches(matrixman, prepared, x_dev) -> dict:
     """One eager forward with CUDA events around every native launch."""
-    from matrixman_b200 import profiling
+    from matrixman_b200 import telemetry as profiling
     cfg = matrixman.config
     old_graphs, old_timing = cfg.cudaGraphs, cfg.gpuTiming
     cfg.cuda_graphs = False
@@ -176,7 +176,8 @@ def run_b200(args):
 
     import matrixman_b200 as matrixman
     import workloads as W
-    from matrixman_b200 import profiling, runtime
+    from matrixman_b200 import runtime
+    from matrixman_b200 import telemetry as profiling
     from workloads.yolov8 import macs_per_image
 
     world, rank, local = dist_env()
@@ -225,7 +226,8 @@ def run_b200(args):
 
     # End to end: pinned host input -> public API -> .cpu() of the result.
     e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
-    x_pinned = x_host.pin_memory() if torch.cuda.is_available() else x_host
+    x_pinned = matrixman.pinned_empty(x_host.shape)
+    x_pinned.copy_(x_host)
     with torch.no_grad():
         for _ in range(2):
             prepared(matrixman.to_device(x_pinned, device=local)).cpu()

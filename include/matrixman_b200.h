@@ -237,6 +237,9 @@ int mm_enable_peer_access(int device, int peer);
 /* Page-locked host buffers for asynchronous transfers. */
 int mm_host_alloc_pinned(size_t bytes, void** out);
 int mm_host_free_pinned(void* ptr);
+/* 1 in *out when ptr lies in page-locked host memory (torch's
+ * Tensor.is_pinned() on the matrixman backend). */
+int mm_host_is_pinned(const void* ptr, int* out);
 
 /* ------------------------------------------------------------------------ */
 /* CUDA graphs (prepared-model execution)                                    */

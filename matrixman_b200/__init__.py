@@ -20,6 +20,7 @@ from .api import (
     get_backend,
     gpu_postprocess_detection,
     init,
+    pinned_empty,
     prefer,
     randn,
     raw_texture,
@@ -48,17 +49,17 @@ def is_gm45_tensor(value) -> bool:
 
 
 def profile_enabled() -> bool:
-    from . import profiling
+    from . import telemetry as profiling
     return profiling.enabled()
 
 
 def profile_report(frame_count: int | None = None) -> str:
-    from . import profiling
+    from . import telemetry as profiling
     return profiling.report(frame_count)
 
 
 def profile_reset() -> None:
-    from . import profiling
+    from . import telemetry as profiling
     profiling.reset()
 
 

@@ -150,6 +150,7 @@ SIGNATURES = {
     "mm_enable_peer_access": [_i, _i],
     "mm_host_alloc_pinned": [_sz, ctypes.POINTER(_vp)],
     "mm_host_free_pinned": [_vp],
+    "mm_host_is_pinned": [_vp, ctypes.POINTER(_i)],
     "mm_graph_capture_begin": [_i, _vp],
     "mm_graph_capture_end": [_i, _vp, ctypes.POINTER(_vp)],
     "mm_graph_launch": [_vp, _vp],

@@ -56,6 +56,8 @@ def get_backend() -> Backend:
         if config.backend not in ("auto", "cuda"):
             raise RuntimeError(f"MatrixMan backend {config.backend!r} is unavailable on this build")
         install_privateuse1_factory_kernels()
+        from .privateuse import register_native_hooks
+        register_native_hooks()  # C++ DeviceGuard + hooks (indexing, pin_memory)
         rt = runtime.get_runtime(runtime.current_device())
         _banner(rt)
         _backend = Backend()
@@ -123,6 +125,29 @@ def randn(*shape: int, seed: int | None = None) -> MatrixManTensor:
     if len(shape) == 1:
         shape = (shape[0], shape[0])
     return tensor(torch.randn(shape, dtype=torch.float32, generator=generator))
+
+
+def pinned_empty(shape, dtype=torch.float32) -> torch.Tensor:
+    """A CPU tensor in page-locked memory (cudaHostAlloc), freed with the tensor.
+
+    Uploads from such buffers are asynchronous copy-engine transfers."""
+    import ctypes
+    import weakref
+
+    from . import _lib
+    lib = _lib.load()
+    shape = tuple(int(s) for s in shape)
+    n = 1
+    for s in shape:
+        n *= s
+    nbytes = max(n, 1) * torch.empty((), dtype=dtype).element_size()
+    ptr = ctypes.c_void_p()
+    _lib.check(lib.mm_host_alloc_pinned(nbytes, ctypes.byref(ptr)), "pinned host allocation")
+    buf = (ctypes.c_uint8 * nbytes).from_address(ptr.value)
+    t = torch.frombuffer(buf, dtype=dtype, count=max(n, 1))[:n].view(shape)
+    weakref.finalize(buf, lib.mm_host_free_pinned, ctypes.c_void_p(ptr.value))
+    t._matrixman_pinned_buffer = buf  # keeps the mapping alive with the tensor
+    return t
 
 
 def synchronize(device=None) -> None:

@@ -610,6 +610,20 @@ extern "C" int mm_host_free_pinned(void* ptr) {
   return MM_OK;
 }
 
+extern "C" int mm_host_is_pinned(const void* ptr, int* out) {
+  if (out == nullptr) return fail(MM_ERR_INVALID, "mm_host_is_pinned: null output");
+  *out = 0;
+  if (ptr == nullptr) return MM_OK;
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return MM_OK;
+  }
+  *out = attr.type == cudaMemoryTypeHost ? 1 : 0;
+  return MM_OK;
+}
+
 // ---------------------------------------------------------------------------
 // C ABI: graphs
 // ---------------------------------------------------------------------------

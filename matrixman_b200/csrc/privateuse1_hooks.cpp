@@ -14,6 +14,7 @@
 #include <torch/extension.h>
 
 #include <atomic>
+#include <cstring>
 
 namespace {
 
@@ -46,6 +47,34 @@ void* runtime_stream(int device) {
   return s;
 }
 
+using pin_alloc_fn = int (*)(size_t, void**);
+using pin_free_fn = int (*)(void*);
+using is_pinned_fn = int (*)(const void*, int*);
+
+void free_pinned(void* p) {
+  if (p) resolve<pin_free_fn>("mm_host_free_pinned")(p);
+}
+
+// Page-locked host memory for Tensor.pin_memory() on this backend, so that
+// uploads from pinned buffers run as asynchronous copy-engine transfers.
+class PinnedAllocator final : public c10::Allocator {
+ public:
+  c10::DataPtr allocate(size_t n) override {
+    void* p = nullptr;
+    if (n > 0) {
+      TORCH_CHECK(resolve<pin_alloc_fn>("mm_host_alloc_pinned")(n, &p) == 0,
+                  "matrixman: pinned host allocation of ", n, " bytes failed");
+    }
+    return {p, p, &free_pinned, c10::Device(c10::DeviceType::CPU)};
+  }
+  c10::DeleterFnPtr raw_deleter() const override { return &free_pinned; }
+  void copy_data(void* dst, const void* src, std::size_t count) const override {
+    std::memcpy(dst, src, count);
+  }
+};
+
+PinnedAllocator g_pinned;
+
 class MatrixManHooks final : public at::PrivateUse1HooksInterface {
  public:
   bool isBuilt() const override { return true; }
@@ -54,6 +83,12 @@ class MatrixManHooks final : public at::PrivateUse1HooksInterface {
   c10::Device getDeviceFromPtr(void*) const override {
     return c10::Device(c10::DeviceType::PrivateUse1, (c10::DeviceIndex)t_current_device);
   }
+  bool isPinnedPtr(const void* data) const override {
+    int pinned = 0;
+    resolve<is_pinned_fn>("mm_host_is_pinned")(data, &pinned);
+    return pinned != 0;
+  }
+  c10::Allocator* getPinnedMemoryAllocator() const override { return &g_pinned; }
 };
 
 class MatrixManGuardImpl final : public c10::impl::DeviceGuardImplInterface {

@@ -14,7 +14,8 @@ from __future__ import annotations
 
 import torch
 
-from . import ops, profiling
+from . import ops
+from . import telemetry as profiling
 from .tensor import (
     MatrixManTensor,
     contiguous_strides,
@@ -265,6 +266,21 @@ def _split_with_sizes(x, split_sizes, dim=0):
 def _unbind(x, dim=0):
     d = _norm_dim(dim, x.dim())
     return tuple(_select(x, d, i) for i in range(int(x.shape[d])))
+
+
+@_register(aten.as_strided_.default)
+def _as_strided_(x, size, stride, storage_offset=None):
+    """In-place restride.  Only metadata-equivalent requests are accepted
+    (same sizes; strides may differ only on size-1 dims), which is what ATen's
+    adaptive_avg_pool2d composite issues for 1x1 channels-last outputs."""
+    size = tuple(int(s) for s in size)
+    stride = tuple(int(s) for s in stride)
+    same_offset = storage_offset is None or int(storage_offset) == x._storage_offset
+    if size == tuple(x.shape) and same_offset and all(
+            s == 1 or a == b for s, a, b in zip(size, stride, x._logical_strides)):
+        return x
+    raise NotImplementedError("MatrixMan/CUDA: as_strided_ that changes the memory layout is "
+                              "not implemented")
 
 
 @_register(aten.as_strided.default)

@@ -23,9 +23,10 @@ def _runtime(device):
     return get_runtime(dev.index or 0)
 
 
-def _dtype(dtype):
+def _dtype(dtype, storage_only: bool = False):
+    """float32/int64 for computed factories; any dtype for empty storage."""
     dtype = torch.float32 if dtype is None else dtype
-    if dtype not in (torch.float32, torch.int64):
+    if not storage_only and dtype not in (torch.float32, torch.int64):
         raise NotImplementedError(f"MatrixMan/CUDA: unsupported factory dtype {dtype}")
     return dtype
 
@@ -37,13 +38,13 @@ def _empty_memory_format(size, dtype=None, layout=None, device=None, pin_memory=
     shape = tuple(int(s) for s in size)
     strides = (channels_last_strides(shape) if memory_format is torch.channels_last and len(shape) == 4
                else contiguous_strides(shape))
-    return ops.empty(_runtime(device), shape, strides, _dtype(dtype))
+    return ops.empty(_runtime(device), shape, strides, _dtype(dtype, storage_only=True))
 
 
 def _empty_strided(size, stride, dtype=None, layout=None, device=None, pin_memory=None):
     from . import ops
     return ops.empty(_runtime(device), tuple(int(s) for s in size), tuple(int(s) for s in stride),
-                     _dtype(dtype))
+                     _dtype(dtype, storage_only=True))
 
 
 def _full(size, fill_value, dtype=None, layout=None, device=None, pin_memory=None):

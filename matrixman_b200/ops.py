@@ -14,7 +14,8 @@ import math
 
 import torch
 
-from . import _lib, profiling
+from . import _lib
+from . import telemetry as profiling
 from .config import config
 from .runtime import DeviceRuntime, get_runtime
 from .tensor import (

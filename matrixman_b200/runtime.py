@@ -23,7 +23,19 @@ _lock = threading.Lock()
 _current_device = threading.local()
 
 DTYPE_CODES = {torch.float32: _lib.MM_F32, torch.int64: _lib.MM_I64}
-ELEMENT_SIZE = {torch.float32: 4, torch.int64: 8}
+
+
+class _ElementSize(dict):
+    """Bytes per element for any torch dtype (storage-only tensors such as the
+    uint8 placeholders ATen's batch_norm composite allocates)."""
+
+    def __missing__(self, dtype):
+        size = torch.empty((), dtype=dtype).element_size()
+        self[dtype] = size
+        return size
+
+
+ELEMENT_SIZE = _ElementSize({torch.float32: 4, torch.int64: 8})
 
 
 def any_initialized() -> bool:
@@ -195,7 +207,9 @@ class DeviceRuntime:
             raise RuntimeError("MatrixMan/CUDA: tensor upload requires a contiguous tensor")
         storage = self.new_storage(data.numel(), data.dtype, kind)
         nbytes = data.numel() * data.element_size()
-        pinned = data.is_pinned()
+        flag = ctypes.c_int(0)
+        self.lib.mm_host_is_pinned(ctypes.c_void_p(data.data_ptr()), ctypes.byref(flag))
+        pinned = bool(flag.value)
         # A pageable source is staged by the driver before the call returns; a
         # pinned source is read asynchronously, so the owner keeps it alive.
         if pinned and not sync:

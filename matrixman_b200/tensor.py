@@ -260,7 +260,8 @@ class MatrixManTensor(torch.Tensor):
     # -- C ABI view ---------------------------------------------------------
     @property
     def element_ptr(self) -> int:
-        return self._owner.pointer + self._storage_offset * (4 if self.dtype == torch.float32 else 8)
+        from .runtime import ELEMENT_SIZE
+        return self._owner.pointer + self._storage_offset * ELEMENT_SIZE[self.dtype]
 
     def desc(self) -> _lib.MMTensor:
         return _lib.make_tensor(self.element_ptr, self.shape, self._logical_strides,

@@ -132,8 +132,7 @@ def test_activations_ulp(mm, name, fn, golden):
     ref = fn(x)
     finite = torch.isfinite(ref)
     assert max_ulp(y[finite], ref[finite]) <= ULP_BAR
-    assert torch.equal(torch.isnan(y), torch.isnan(ref))
-    assert torch.equal(y[~finite], ref[~finite])
+    assert bit_exact(y[~finite], ref[~finite])  # inf/nan in the same places (silu(-inf) = nan)
     if name == "silu":
         kat = F.silu(dev(mm, torch.from_numpy(golden["silu_x"]))).cpu()
         assert max_ulp(kat, torch.from_numpy(golden["silu_y"])) <= ULP_BAR
