@@ -346,6 +346,11 @@ int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float* w_lo, int
                  const mm_tensor_t* residual, const mm_conv_params_t* p, const mm_tensor_t* y,
                  void* stream);
 
+/* Error code recorded by a device-side bounded wait that gave up (0 = none);
+ * clear != 0 resets it.  Kernels never trap: a stuck pipeline records the code,
+ * frees its tensor memory and returns, and the host reads the code here. */
+int mm_kernel_error(int device, int* code_out, int clear);
+
 /* Split prepacked weights into the tf32 high part and the fp32 remainder
  * (w_hi = w with its 13 low mantissa bits cleared, w_lo = w - w_hi), in place on
  * the device: n elements of src -> hi, lo. */

@@ -173,6 +173,7 @@ SIGNATURES = {
     "mm_conv2d_tc": [_T, _fp, _fp, _i, _i, _i, _i, _i, _i, _fp, _T,
                      ctypes.POINTER(MMConvParams), _T, _vp],
     "mm_tf32_split": [_fp, _fp, _fp, _i64, _vp],
+    "mm_kernel_error": [_i, ctypes.POINTER(_i), _i],
     "mm_gemm": [_T, _T, _T, _d, _d, _i, _T, _vp],
     "mm_yolo_decode": [_TT, ctypes.POINTER(ctypes.c_float), _i, _i, _i, _T, _vp],
 }

@@ -78,7 +78,7 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
         for f in futs:
             f.result()
     tmp = OUT / (LIB_NAME + ".tmp")
-    cmd = [NVCC, *ARCH, "-shared", "-cudart", "shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+    cmd = [NVCC, *ARCH, "-shared", "-cudart", "shared", "-o", str(tmp), *map(str, objs)]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -395,6 +395,50 @@ def convolution(x, weight, bias, stride, padding, dilation, groups, *, act=_lib.
     return out
 
 
+def conv_tc(x: MatrixManTensor, w_hi: MatrixManTensor, w_lo: MatrixManTensor, k_out: int, c_in: int,
+            r: int, s: int, c_pad: int, k_pad: int, bias, stride, padding, dilation, act,
+            residual, residual_before_act, out: MatrixManTensor) -> bool:
+    """tcgen05 3xTF32 convolution on prepacked hi/lo weight planes.
+
+    Returns False (nothing launched) when the geometry or layout is outside
+    what the tensor-core kernel covers; the caller then runs mm_conv2d."""
+    params = _lib.MMConvParams(stride[0], stride[1], padding[0], padding[1], dilation[0], dilation[1],
+                               1, int(act), 1 if residual_before_act else 0, 2)
+    res_desc = residual.desc() if residual is not None else None
+    name = "mm_conv2d_tc"
+    lib = _lib_handle()
+    stream = x.runtime.stream
+    token = profiling.launch_times.begin(name, stream) if profiling.gpu_timing_enabled() else None
+    status = lib.mm_conv2d_tc(_p(x.desc()), ctypes.c_void_p(w_hi.element_ptr),
+                              ctypes.c_void_p(w_lo.element_ptr), int(k_out), int(c_in), int(r), int(s),
+                              int(c_pad), int(k_pad),
+                              ctypes.c_void_p(bias.element_ptr) if bias is not None else None,
+                              _p(res_desc) if res_desc is not None else None, ctypes.byref(params),
+                              _p(out.desc()), stream)
+    if status == _lib.MM_ERR_UNSUPPORTED:
+        if token is not None:
+            profiling.launch_times.end(token)
+            profiling.launch_times.records.pop()
+        return False
+    _lib.check(status, name)
+    if token is not None:
+        profiling.launch_times.end(token)
+    profiling.count_launch(name)
+    if config.cudaDisableAsyncQueue or config.cudaDebug:
+        x.runtime.synchronize()
+        check_kernel_error(x.runtime.index)
+    return True
+
+
+def check_kernel_error(device: int) -> None:
+    """Raise if a device-side bounded wait gave up (the kernel returned early)."""
+    code = ctypes.c_int(0)
+    _lib.check(_lib_handle().mm_kernel_error(int(device), ctypes.byref(code), 1), "kernel status")
+    if code.value:
+        raise _lib.MatrixManNativeError(
+            f"MatrixMan/CUDA: a tensor-core kernel stopped after a bounded wait (code {code.value})")
+
+
 def gemm(x, w_kn, bias=None, alpha=1.0, beta=1.0, act=_lib.ACT_NONE, out=None) -> MatrixManTensor:
     """out[M,N] = act(alpha * x @ w_kn + beta * bias) (addmm / mm / linear)."""
     x = require_mm(x, "mm")

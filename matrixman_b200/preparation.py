@@ -208,6 +208,15 @@ def _channel_slice(buf: MatrixManTensor, start: int, stop: int) -> MatrixManTens
                                        buf._logical_strides)
 
 
+def tf32_round_nearest(x: torch.Tensor) -> torch.Tensor:
+    """Round fp32 values to tf32 (10-bit mantissa), nearest with ties away from
+    zero: add half a tf32 ulp to the magnitude bits, then clear the 13 low bits
+    (a carry into the exponent is the correct rounding).  Finite inputs only."""
+    bits = x.contiguous().view(torch.int32)
+    rounded = (bits + 0x1000) & -8192
+    return rounded.view(torch.float32)
+
+
 class PreparedConv2d(nn.Module):
     """Conv2d (+ folded BN) + activation (+ residual) as one fused kernel.
 
@@ -240,29 +249,62 @@ class PreparedConv2d(nn.Module):
         return (f"{self.in_channels}, {self.out_channels}, kernel=({self.kh}, {self.kw}), "
                 f"stride={self.stride}, padding={self.padding}, groups={self.groups}, act={act}")
 
+    @property
+    def tc_eligible(self) -> bool:
+        """The tcgen05 kernel covers ungrouped convolutions with C % 4 == 0."""
+        return self.groups == 1 and self.in_channels % 4 == 0
+
+    def tc_planes(self) -> tuple[torch.Tensor, torch.Tensor, int, int]:
+        """[K_pad, R*S*C_pad] tf32 high part and fp32 remainder of the weights
+        (C padded to a multiple of 32, K to a multiple of 16, zeros)."""
+        k, r, s, c = (int(v) for v in self.weight_krsc.shape)
+        c_pad = (c + 31) // 32 * 32
+        k_pad = (k + 15) // 16 * 16
+        packed = torch.zeros(k_pad, r, s, c_pad, dtype=torch.float32)
+        packed[:k, :, :, :c] = self.weight_krsc
+        packed = packed.reshape(k_pad, r * s * c_pad).contiguous()
+        hi = tf32_round_nearest(packed)
+        lo = packed - hi
+        return hi.contiguous(), lo.contiguous(), c_pad, k_pad
+
     def device_weights(self, rt):
         entry = self._device_weights.get(rt.index)
         if entry is None:
-            from .runtime import DeviceStorage  # noqa: F401 (type)
             w_store = rt.upload(self.weight_krsc, kind=_lib.POOL_PARAMETER, sync=True)
             k, r, s, c = (int(v) for v in self.weight_krsc.shape)
             w_view = MatrixManTensor(w_store, (k, c, r, s), 0, (r * s * c, 1, s * c, c))
             b_store = rt.upload(self.bias, kind=_lib.POOL_PARAMETER, sync=True)
             b_view = MatrixManTensor(b_store, (k,), 0, (1,))
-            entry = (w_view, b_view)
+            tc = None
+            if self.tc_eligible:
+                hi, lo, c_pad, k_pad = self.tc_planes()
+                hs = rt.upload(hi, kind=_lib.POOL_PARAMETER, sync=True)
+                ls = rt.upload(lo, kind=_lib.POOL_PARAMETER, sync=True)
+                tc = (MatrixManTensor(hs, tuple(hi.shape), 0, (hi.shape[1], 1)),
+                      MatrixManTensor(ls, tuple(lo.shape), 0, (lo.shape[1], 1)), c_pad, k_pad)
+            entry = (w_view, b_view, tc)
             self._device_weights[rt.index] = entry
         return entry
 
     def forward(self, x, out=None, residual=None, residual_before_act=False):
         if not isinstance(x, MatrixManTensor):
             raise RuntimeError("PreparedConv2d requires a MatrixMan CUDA tensor")
-        w, b = self.device_weights(x.runtime)
+        w, b, tc = self.device_weights(x.runtime)
         if out is None:
             n, _, h, wd = (int(v) for v in x.shape)
             oh, ow = ops.conv_output_hw(h, wd, self.kh, self.kw, self.stride, self.padding,
                                         self.dilation)
             shape = (n, self.out_channels, oh, ow)
             out = ops.empty(x.runtime, shape, _nhwc(shape))
+        if tc is not None and config.convAlgo != "simt" and not config.cudaDisableSpecializedConv:
+            hi, lo, c_pad, k_pad = tc
+            if ops.conv_tc(x, hi, lo, self.out_channels, self.in_channels, self.kh, self.kw, c_pad,
+                           k_pad, b, self.stride, self.padding, self.dilation, self.act, residual,
+                           residual_before_act, out):
+                return out
+            if config.convAlgo == "tc":
+                raise NotImplementedError("MatrixMan/CUDA: conv_algo='tc' but this convolution's "
+                                          "layout is not covered by the tensor-core kernel")
         return ops.convolution(x, w, b, self.stride, self.padding, self.dilation, self.groups,
                                act=self.act, residual=residual,
                                residual_before_act=residual_before_act, out=out)

@@ -1,0 +1,120 @@
+"""Parity of the tcgen05 3xTF32 convolution (prepared units) with the CPU
+oracle, across the geometries YOLOv8 / ResNet use plus edge cases."""
+
+import pytest
+import torch
+from torch import nn
+
+from matrixman_b200 import _lib
+from matrixman_b200.preparation import PreparedConv2d
+from oracle import ops as O
+from oracle.tolerance import CONV_GEMM_REL, max_rel_err
+
+pytestmark = pytest.mark.gpu
+
+ACTS = {0: lambda t: t, 1: torch.relu, 2: torch.nn.functional.silu}
+
+
+def gen(seed):
+    g = torch.Generator()
+    g.manual_seed(seed)
+    return g
+
+
+def nhwc(mm, t):
+    return mm.to_device(t.permute(0, 2, 3, 1).contiguous()).permute(0, 3, 1, 2)
+
+
+def run_case(mm, n, c, k, ksz, stride, pad, hw, act=2, residual=None, seed=0):
+    g = gen(seed)
+    conv = nn.Conv2d(c, k, ksz, stride, pad, bias=True)
+    with torch.no_grad():
+        conv.weight.copy_(torch.randn(conv.weight.shape, generator=g) / (c * ksz * ksz) ** 0.5)
+        conv.bias.copy_(torch.randn(k, generator=g) * 0.1)
+    unit = PreparedConv2d(conv, act)
+    assert unit.tc_eligible
+    x = torch.rand(n, c, hw, hw + 3, generator=g) * 2 - 1
+    ref = ACTS[act](O.conv2d(x, conv.weight.detach(), conv.bias.detach(), stride, pad))
+    res_dev = None
+    if residual is not None:
+        r = torch.randn(ref.shape, generator=g)
+        res_dev = nhwc(mm, r)
+        if residual == "before":
+            ref = ACTS[act](O.conv2d(x, conv.weight.detach(), conv.bias.detach(), stride, pad) + r)
+        else:
+            ref = ref + r
+    from matrixman_b200 import telemetry
+    before = telemetry.launches["mm_conv2d_tc"]
+    y = unit(nhwc(mm, x), residual=res_dev, residual_before_act=residual == "before")
+    assert telemetry.launches["mm_conv2d_tc"] == before + 1, "tensor-core path did not run"
+    err = max_rel_err(y.cpu(), ref)
+    assert err < CONV_GEMM_REL, f"max relative error {err:.3g}"
+    return err
+
+
+@pytest.mark.parametrize("n,c,k,ksz,stride,pad,hw", [
+    (2, 16, 32, 3, 2, 1, 40),     # YOLO downsample
+    (2, 32, 32, 3, 1, 1, 20),     # bottleneck 3x3
+    (1, 64, 64, 1, 1, 0, 33),     # 1x1
+    (1, 48, 80, 3, 1, 1, 17),     # detect class branch width
+    (1, 4, 5, 3, 1, 1, 64),       # config-1 channel counts (C padded to 32)
+    (1, 128, 144, 1, 1, 0, 12),   # K not a multiple of 16 tile
+    (1, 96, 576, 3, 2, 1, 10),    # K > 256: three N tiles
+    (3, 256, 256, 3, 1, 1, 7),    # deep layer
+    (1, 64, 64, 7, 2, 3, 23),     # 7x7 stride 2
+])
+def test_tc_conv_geometries(mm, n, c, k, ksz, stride, pad, hw):
+    run_case(mm, n, c, k, ksz, stride, pad, hw, act=2, seed=c * 7 + k)
+
+
+@pytest.mark.parametrize("act", [0, 1, 2])
+@pytest.mark.parametrize("residual", [None, "before", "after"])
+def test_tc_conv_epilogues(mm, act, residual):
+    run_case(mm, 2, 32, 48, 3, 1, 1, 15, act=act, residual=residual, seed=act * 3 + len(str(residual)))
+
+
+def test_tc_precision_is_fp32_class(mm):
+    """3xTF32 must be far below the 1e-4 bar (plain tf32 would be ~1e-3)."""
+    err = run_case(mm, 1, 64, 64, 3, 1, 1, 32, act=0, seed=5)
+    assert err < 1e-5
+
+
+def test_tc_channel_slices_in_and_out(mm):
+    from matrixman_b200 import ops
+    from matrixman_b200.preparation import _channel_slice
+    g = gen(9)
+    conv = nn.Conv2d(16, 32, 3, 1, 1)
+    unit = PreparedConv2d(conv, 2)
+    big = torch.randn(2, 48, 9, 11, generator=g)
+    xd = nhwc(mm, big)
+    xin = _channel_slice(xd, 16, 32)
+    out_buf = ops.empty(xd.runtime, (2, 96, 9, 11), (96 * 9 * 11, 1, 11 * 96, 96))
+    ops.fill_(out_buf, 0.0)
+    unit(xin, out=_channel_slice(out_buf, 32, 64))
+    y = out_buf.cpu()
+    ref = torch.nn.functional.silu(O.conv2d(big[:, 16:32], conv.weight.detach(), conv.bias.detach(), 1, 1))
+    assert max_rel_err(y[:, 32:64], ref) < CONV_GEMM_REL
+    assert torch.count_nonzero(y[:, :32]) == 0 and torch.count_nonzero(y[:, 64:]) == 0
+
+
+def test_tc_matches_simt_path(mm):
+    import matrixman_b200 as matrixman
+    g = gen(11)
+    conv = nn.Conv2d(64, 64, 3, 1, 1)
+    unit = PreparedConv2d(conv, 2)
+    x = nhwc(mm, torch.randn(2, 64, 20, 20, generator=g))
+    y_tc = unit(x).cpu()
+    old = matrixman.config.conv_algo
+    matrixman.config.conv_algo = "simt"
+    try:
+        y_simt = unit(x).cpu()
+    finally:
+        matrixman.config.conv_algo = old
+    assert max_rel_err(y_tc, y_simt) < 1e-5
+
+
+def test_no_kernel_error_recorded(mm):
+    import ctypes
+    code = ctypes.c_int(-1)
+    _lib.check(_lib.load().mm_kernel_error(0, ctypes.byref(code), 0))
+    assert code.value == 0

@@ -90,6 +90,18 @@ def test_fold_equivalence_on_cpu():
         assert torch.allclose(bn(conv(x)), nn.functional.conv2d(x, w, b, padding=1), atol=1e-5, rtol=1e-5)
 
 
+def test_tf32_split_is_exact_and_round_nearest():
+    from matrixman_b200.preparation import tf32_round_nearest
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(100000, generator=g) * torch.exp(torch.randn(100000, generator=g) * 5)
+    hi = tf32_round_nearest(x)
+    lo = x - hi
+    assert torch.all((hi.view(torch.int32) & 0x1FFF) == 0)
+    assert torch.equal(hi + lo, x)  # the split is exact
+    ulp = torch.ldexp(torch.ones_like(x), torch.frexp(x)[1] - 11)  # tf32 ulp of |x|
+    assert torch.all(lo.abs() <= ulp / 2)
+
+
 def test_prepacked_layouts():
     conv = nn.Conv2d(8, 16, 3, padding=1, bias=False)
     unit = PreparedConv2d(conv, 2)
