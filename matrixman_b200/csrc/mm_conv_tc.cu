@@ -4,24 +4,33 @@
 // (tap r, tap s, channel c) with channels padded to C_pad (multiple of 32).
 //
 // Persistent CTAs (one per SM) walk a static list of 128-pixel x BN-channel
-// tiles.  Warp roles:
-//   * warps 0-7 (A producers): gather 128 pixel rows x 32 channels per k-block
-//     with 16-byte loads (zero for padding taps, out-of-range pixels and padded
-//     channels), prefetching the next k-block into registers while the current
-//     one is split into a tf32 high part (round to nearest) and the exact fp32
-//     remainder and stored into 128B-swizzled K-major stage buffers;
+// tiles (BN <= 80).  Warp roles:
+//   * warps 0-7 (A producers, two per TMEM lane quarter): copy their 32 pixel
+//     rows x 16 channels of every 32-channel k-block with 16-byte cp.async
+//     into a private 4-deep shared-memory ring that runs ahead across tile
+//     boundaries (zero-fill for padding taps, rows past the end and padded
+//     channels), split each value into a tf32 high part (round to nearest) and
+//     the exact fp32 remainder, and write both planes into a TMEM A stage with
+//     tcgen05.st -- so the MMAs read only the weights from shared memory;
 //   * warp 8 (TMA): prepacked [K_pad][R*S*C_pad] weight hi/lo planes, one 2-D
 //     tiled load each per stage (no multicast);
-//   * warp 9 (MMA): one thread issues, per 8-wide k step, three
-//     tcgen05.mma.kind::tf32 (A_hi*B_hi + A_hi*B_lo + A_lo*B_hi) into one of two
-//     TMEM period buffers; every `period` k-blocks the buffer is handed over;
-//   * warps 10-13 (accumulator): add each finished period into an fp32 total
-//     kept in TMEM with round-to-nearest adds -- the tensor core's own
-//     accumulation rounds toward zero, so long reductions inside TMEM drift by
-//     ~K * 2^-24 -- and, after the last period, apply bias, activation and the
-//     optional residual and store the NHWC output (possibly a channel slice of
-//     a concat buffer).  This overlaps the epilogue of one tile with the MMAs
-//     of the next.
+//   * warps 9, 10, 11 (MMA issue, one thread each): A_hi*B_hi, A_hi*B_lo and
+//     A_lo*B_hi, four tcgen05.mma.kind::tf32 per k-block each, into separate
+//     TMEM accumulators.  Three issuing threads overlap the per-instruction
+//     issue latency that bounds a single issuer at small N.  The hi*hi sum
+//     alternates between two period buffers handed over every `period`
+//     k-blocks; the two cross terms (~2^-11 of the result) accumulate a whole
+//     tile each;
+//   * warps 12-19 (accumulator, two per lane quarter): add each finished
+//     hi*hi period into an fp32 total held in registers with round-to-nearest
+//     adds -- the tensor core's own accumulation rounds toward zero, so long
+//     reductions inside TMEM drift by ~K * 2^-24 -- then add the cross terms
+//     and apply bias (staged in shared memory), activation and the optional
+//     residual, and store the NHWC output (possibly a channel slice of a
+//     concat buffer).  The epilogue of one tile overlaps the MMAs of the next.
+//
+// Stage and phase counters advance incrementally (no divisions in the
+// per-k-block paths), and per-row input offsets are computed once per tile.
 //
 // Every wait is bounded: on timeout the kernel records an error code in
 // g_tc_error (read with mm_kernel_error), stops issuing work, waits for its
@@ -211,26 +220,36 @@ struct TcArgs {
   int h, w, c;
   int oh, ow, kout;
   int r, s, sh, sw, ph, pw, dh, dw;
-  int64_t m_total;
+  int m_total;    // output pixels (fits in 31 bits; checked on the host)
   int kb_total;  // r * s * (c_pad / 32)
   int cb;        // c_pad / 32
-  int bn;        // N tile: multiple of 16, <= 128
+  int bn;        // N tile: multiple of 16, <= TC_MAX_BN
   int n_tiles;   // ceil(kout / bn)
   int64_t tiles; // m tiles * n tiles
-  int stages;
-  int period;    // k-blocks accumulated in TMEM before promotion to the fp32 total
+  int stages;    // pipeline depth (TMEM A stages == shared-memory B stages)
+  int period;    // k-blocks of hi*hi products accumulated in TMEM before promotion
   int act, res_before_act;
   int vec_store;  // output rows 16-byte aligned: float4 stores
-  uint32_t tmem_cols;
+  int res_vec;    // residual rows 16-byte aligned: float4 loads
 };
 
 // Warp roles of the persistent kernel.
-constexpr int TC_A_WARPS = 8;                 // warps 0-7: A producers
-constexpr int TC_WARP_TMA = 8;                // warp 8: weight TMA
-constexpr int TC_WARP_MMA = 9;                // warp 9: MMA issue + TMEM owner
-                                              // warps 10-13: promotion + epilogue
-constexpr int TC_V2_THREADS = 14 * 32;
-constexpr int TC_A_ROWS = TC_BM / (TC_A_WARPS * 32 / 8);  // rows per producer thread (4)
+constexpr int TC_A_WARPS = 8;      // warps 0-7: A producers (2 per TMEM lane quarter)
+constexpr int TC_WARP_TMA = 8;     // warp 8: weight TMA
+constexpr int TC_WARP_HH = 9;      // warp 9: hi*hi MMA issue + TMEM owner
+constexpr int TC_WARP_HL = 10;     // warp 10: hi*lo MMA issue
+constexpr int TC_WARP_LH = 11;     // warp 11: lo*hi MMA issue
+constexpr int TC_WARP_EPI = 12;    // warps 12-19: promotion + epilogue (2 per lane quarter)
+constexpr int TC_EPI_WARPS = 8;
+constexpr int TC_EPI_CHUNKS = 3;   // 16-column chunks per epilogue warp (bn <= 96)
+constexpr int TC_THREADS = (TC_WARP_EPI + TC_EPI_WARPS) * 32;
+constexpr int TC_STG_DEPTH = 4;    // k-blocks of A copies in flight per producer warp (power of 2)
+constexpr int TC_STG_SLOT = 32 * 64;  // one k-block of a producer warp: 32 rows x 64 B
+constexpr uint32_t TC_TMEM_COLS = 512;
+constexpr int TC_A_COLS = 64;      // TMEM columns per A stage (32 hi + 32 lo)
+constexpr int TC_MAX_BN = 80;      // N tile limit: 4 accumulators of bn columns + 3 A stages
+constexpr int TC_MAX_STAGES = 6;
+constexpr int TC_MAX_BIAS = 2048;  // output channels whose bias is staged in shared memory
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
   asm volatile(
@@ -245,23 +264,149 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
       : "memory");
 }
 
-__global__ void __launch_bounds__(TC_V2_THREADS, 1)
+// tcgen05.ld of 16 columns without the completion wait (callers batch loads
+// and issue one tcgen05.wait::ld).
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// MMA with the A operand (128 x 8 tf32) read from tensor memory.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                            uint32_t idesc, uint32_t accumulate) {
+  uint32_t mask = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask)
+      : "memory");
+}
+
+// Shared-memory layout of one CTA (offsets from the 1024-aligned base).
+struct TcSmem {
+  uint32_t stage_bytes, staging, bias, bars;
+  int stages;
+  __host__ __device__ static TcSmem make(int bn, int stages, int kout) {
+    TcSmem l;
+    l.stages = stages;
+    l.stage_bytes = 2u * (uint32_t)bn * 128u;           // B hi + lo tiles
+    l.staging = (uint32_t)stages * l.stage_bytes;        // A copy rings of the producer warps
+    l.bias = l.staging + TC_A_WARPS * TC_STG_DEPTH * TC_STG_SLOT;       // kout floats, 16-byte padded
+    l.bars = l.bias + (((uint32_t)kout * 4u + 15u) & ~15u);
+    return l;
+  }
+  // mbarriers: full_a[S], full_b[S], empty[S], hh_full[2], hh_free[2],
+  // cross_full, cross_free, drain[3]; then the TMEM address slot.
+  __host__ __device__ int n_bars() const { return 3 * stages + 9; }
+  __host__ __device__ size_t bytes() const { return 1024 + bars + (size_t)n_bars() * 8 + 16; }
+};
+
+// One MMA issuer.  ROLE 0 (hi*hi) rotates between two period buffers that the
+// promotion warps fold into the fp32 total every `period` k-blocks; ROLE 1
+// (hi*lo) and ROLE 2 (lo*hi) accumulate a whole tile into one buffer each --
+// their partial sums are ~2^-11 of the result, so the tensor core's
+// round-toward-zero accumulation leaves no measurable drift there.
+template <int ROLE>
+__device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const TcSmem& L,
+                                         uint32_t tmem, uint64_t* full_a, uint64_t* full_b,
+                                         uint64_t* empty, uint64_t* hh_full, uint64_t* hh_free,
+                                         uint64_t* cross_full, uint64_t* cross_free,
+                                         uint64_t* drain) {
+  const int S = a.stages, KB = a.kb_total;
+  const int NP = (KB + a.period - 1) / a.period;
+  const uint32_t b_bytes = (uint32_t)a.bn * 128;
+  const uint32_t acc0 = (uint32_t)(TC_A_COLS * S);
+  const uint32_t idesc = idesc_tf32(TC_BM, a.bn);
+  const uint32_t a_off = ROLE == 2 ? 32u : 0u;         // A lo plane for lo*hi
+  const uint32_t b_off = ROLE == 1 ? b_bytes : 0u;     // B lo plane for hi*lo
+  int64_t pc = 0, tc = 0;
+  int st = 0;         // A/B stage of the next k-block
+  uint32_t par = 0;   // its fill phase parity
+  bool alive = true;
+  for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x, ++tc) {
+    uint32_t d = tmem + acc0 + (uint32_t)((ROLE == 1 ? 2 : 3) * a.bn);
+    if (ROLE != 0) {
+      if (!mbar_wait(cross_free, (uint32_t)(tc & 1) ^ 1u, TC_ERR_WAIT_ACC)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+    }
+    for (int p = 0; p < NP && alive; ++p) {
+      if (ROLE == 0) {
+        const int b = (int)(pc & 1);
+        if (!mbar_wait(&hh_free[b], (uint32_t)((pc >> 1) & 1) ^ 1u, TC_ERR_WAIT_ACC)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        d = tmem + acc0 + (uint32_t)(b * a.bn);
+      }
+      const int kb_begin = p * a.period;
+      const int kb_end = min(KB, kb_begin + a.period);
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
+        if (!mbar_wait(&full_a[st], par, TC_ERR_WAIT_A) ||
+            !mbar_wait(&full_b[st], par, TC_ERR_WAIT_B)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t at = tmem + (uint32_t)(st * TC_A_COLS) + a_off;
+        const uint32_t bs = smem_addr(smem + (size_t)st * L.stage_bytes) + b_off;
+        const bool first = ROLE == 0 ? kb == kb_begin : kb == 0;
+#pragma unroll
+        for (int k = 0; k < TC_BK / 8; ++k)
+          mma_tf32_ts(d, at + 8 * k, smem_desc_sw128(bs + 32 * k), idesc, (first && k == 0) ? 0u : 1u);
+        mma_commit(&empty[st]);
+        if (++st == S) {
+          st = 0;
+          par ^= 1u;
+        }
+      }
+      if (ROLE == 0 && alive) {
+        mma_commit(&hh_full[pc & 1]);  // arrives once the period's MMAs have completed
+        ++pc;
+      }
+    }
+    if (ROLE != 0 && alive) mma_commit(cross_full);
+  }
+  if (!alive || tc_error_raised()) {
+    // Error path: no MMA of this thread may still write TMEM when it is freed.
+    mma_commit(&drain[ROLE]);
+    mbar_wait(&drain[ROLE], 0u, TC_ERR_WAIT_ACC);
+  }
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap_hi,
                    const __grid_constant__ CUtensorMap wmap_lo, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int S = a.stages;
-  const uint32_t a_bytes = TC_BM * 128;
+  const TcSmem L = TcSmem::make(a.bn, S, a.kout);
+  float* bias_s = (float*)(smem + L.bias);
   const uint32_t b_bytes = (uint32_t)a.bn * 128;
-  const uint32_t stage_bytes = 2 * a_bytes + 2 * b_bytes;
-  uint64_t* bars = (uint64_t*)(smem + (size_t)S * stage_bytes);
-  uint64_t* full_a = bars;            // S: 256 producer arrivals
-  uint64_t* full_b = bars + S;        // S: TMA transaction bytes
-  uint64_t* empty = bars + 2 * S;     // S: MMA commit frees the stage
-  uint64_t* buf_full = bars + 3 * S;  // 2: MMA commit, a period is in TMEM
-  uint64_t* buf_free = bars + 3 * S + 2;  // 2: 128 promotion arrivals
-  uint64_t* drain = bars + 3 * S + 4;     // 1: MMA error path waits for its MMAs
-  uint32_t* tmem_slot = (uint32_t*)(bars + 3 * S + 5);
+  uint8_t* staging = smem + L.staging;
+  uint64_t* bars = (uint64_t*)(smem + L.bars);
+  uint64_t* full_a = bars;                // S: 256 producer arrivals (A stage written to TMEM)
+  uint64_t* full_b = bars + S;            // S: TMA transaction bytes
+  uint64_t* empty = bars + 2 * S;         // S: one commit per issuer frees the A/B stage
+  uint64_t* hh_full = bars + 3 * S;       // 2: hi*hi period complete in TMEM
+  uint64_t* hh_free = bars + 3 * S + 2;   // 2: one arrival per promotion thread
+  uint64_t* cross_full = bars + 3 * S + 4;  // hi*lo and lo*hi tile sums complete
+  uint64_t* cross_free = bars + 3 * S + 5;  // one arrival per epilogue thread
+  uint64_t* drain = bars + 3 * S + 6;       // 3: issuer error paths wait for their MMAs
+  uint32_t* tmem_slot = (uint32_t*)(bars + L.n_bars());
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   __shared__ int s_skip;
@@ -273,247 +418,311 @@ __global__ void __launch_bounds__(TC_V2_THREADS, 1)
     for (int i = 0; i < S; ++i) {
       mbar_init(&full_a[i], TC_A_WARPS * 32);
       mbar_init(&full_b[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], 3);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&buf_full[i], 1);
-      mbar_init(&buf_free[i], 128);
+      mbar_init(&hh_full[i], 1);
+      mbar_init(&hh_free[i], 32 * TC_EPI_WARPS);
     }
-    mbar_init(drain, 1);
+    mbar_init(cross_full, 2);
+    mbar_init(cross_free, 32 * TC_EPI_WARPS);
+    for (int i = 0; i < 3; ++i) mbar_init(&drain[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == TC_WARP_MMA) {
+  if (warp == TC_WARP_HH) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_slot)),
-                 "r"(a.tmem_cols)
+                 "r"(TC_TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  if (a.bias)
+    for (int i = threadIdx.x; i < a.kout; i += TC_THREADS) bias_s[i] = a.bias[i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: period buffers at [0, bn) and [bn, 2 bn), fp32 total at [2 bn, 3 bn).
+  // TMEM columns: A stages at [64 s, 64 s + 64) (hi then lo); from acc0 = 64 S
+  // the hi*hi period buffers [acc0, acc0 + 2 bn), the hi*lo tile sum
+  // [acc0 + 2 bn, acc0 + 3 bn) and the lo*hi tile sum [acc0 + 3 bn, acc0 + 4 bn).
+  const uint32_t acc0 = (uint32_t)(TC_A_COLS * S);
   const int KB = a.kb_total;
   const int NP = (KB + a.period - 1) / a.period;
 
   if (warp < TC_A_WARPS) {
-    // ---------------- A producers: gather, split, store (register prefetch) --------------
-    const int t = threadIdx.x;
-    const int j = t & 7;
-    const int row0 = t >> 3;  // 0..31; rows row0 + 32 i
-    const uint32_t swz = (uint32_t)((j ^ (row0 & 7)) << 4);
-    int64_t g = 0;  // global k-block counter across tiles
-    bool alive = true;
-    for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x) {
-      const int64_t m0 = (tile / a.n_tiles) * TC_BM;
-      int64_t base[TC_A_ROWS];
-      int ih0[TC_A_ROWS], iw0[TC_A_ROWS];
-      bool rowok[TC_A_ROWS];
+    // ---------------- A producers: cp.async gather -> split -> TMEM ----------------
+    // Warp w owns TMEM lane quarter q = w % 4 (tile rows 32 q .. 32 q + 31) and
+    // channel half h = w / 4 of every 32-channel k-block.  Each k-block's 32
+    // rows x 64 B arrive by 16-byte cp.async (zero-filled for padding taps,
+    // rows past the end and padded channels) in a private ring of
+    // TC_STG_DEPTH slots that runs ahead across tile boundaries; a slot is
+    // XOR swizzled so both the copies (8 rows x 64 B) and the per-row reads
+    // are conflict-free.  Each lane then splits its row into tf32 high part
+    // and exact remainder and writes both planes to the TMEM A stage.
+    const int q = warp & 3;
+    const int half = warp >> 2;
+    const int lrow = lane >> 2;
+    const int lchunk = lane & 3;
+    const uint32_t stg = smem_addr(staging + warp * (TC_STG_DEPTH * TC_STG_SLOT));
+    const uint32_t tm_rows = tmem + ((uint32_t)(q * 32) << 16);
+    const int64_t my_tiles = a.tiles > blockIdx.x ? (a.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int64_t total = my_tiles * KB;
+    // Prefetch cursor: tile, k-block position (tap r, tap s, channel block) and
+    // the per-row input coordinates of that tile.  Row offsets include this
+    // lane's channel offset; a k-block adds one offset uniform over the warp.
+    int64_t ptile = blockIdx.x;
+    int pkr = 0, pks = 0, pcb = 0;
+    const int lane_c = half * 16 + lchunk * 4;
+    int64_t roff[4];
+    int ih0[4], iw0[4];
+    auto setup_rows = [&]() {
+      const int m0 = (int)(ptile / a.n_tiles) * TC_BM + q * 32;
 #pragma unroll
-      for (int i = 0; i < TC_A_ROWS; ++i) {
-        const int64_t m = m0 + row0 + 32 * i;
-        rowok[i] = m < a.m_total;
-        const int64_t mm_ = rowok[i] ? m : 0;
-        const int ow_ = (int)(mm_ % a.ow);
-        const int64_t q = mm_ / a.ow;
-        const int oh_ = (int)(q % a.oh);
-        base[i] = (q / a.oh) * a.xs0;
-        ih0[i] = oh_ * a.sh - a.ph;
+      for (int i = 0; i < 4; ++i) {
+        const int m = m0 + lrow + 8 * i;
+        const bool ok = m < a.m_total;
+        const unsigned mm_ = ok ? (unsigned)m : 0u;
+        const int ow_ = (int)(mm_ % (unsigned)a.ow);
+        const unsigned qq = mm_ / (unsigned)a.ow;
+        const int oh_ = (int)(qq % (unsigned)a.oh);
+        // Rows past the end get a coordinate that fails the bounds test.
+        ih0[i] = ok ? oh_ * a.sh - a.ph : -0x40000000;
         iw0[i] = ow_ * a.sw - a.pw;
+        roff[i] = (int64_t)(qq / (unsigned)a.oh) * a.xs0 + (int64_t)ih0[i] * a.xs2 +
+                  (int64_t)iw0[i] * a.xs3 + lane_c;
       }
-      float4 nxt[TC_A_ROWS];
-      auto fetch = [&](int kb, float4* v) {
-        const int tap = kb / a.cb;
-        const int cbk = kb - tap * a.cb;
-        const int kr = tap / a.s, ks = tap - kr * a.s;
-        const int c = cbk * TC_BK + j * 4;
+    };
+    // Issue the copies of the cursor's k-block into `slot` and advance it.
+    auto prefetch = [&](int slot) {
+      const int dy = pkr * a.dh, dx = pks * a.dw;
+      const int cbase = pcb * TC_BK;
+      const bool cok = cbase + lane_c < a.c;
+      const int64_t koff = (int64_t)dy * a.xs2 + (int64_t)dx * a.xs3 + cbase;
+      const uint32_t sbase = stg + slot * TC_STG_SLOT;
 #pragma unroll
-        for (int i = 0; i < TC_A_ROWS; ++i) {
-          const int ih = ih0[i] + kr * a.dh, iw = iw0[i] + ks * a.dw;
-          const bool ok = rowok[i] && c < a.c && ih >= 0 && ih < a.h && iw >= 0 && iw < a.w;
-          v[i] = ok ? __ldg(reinterpret_cast<const float4*>(a.x + base[i] + (int64_t)ih * a.xs2 +
-                                                             (int64_t)iw * a.xs3 + c))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = 0; i < 4; ++i) {
+        const int row = lrow + 8 * i;
+        const bool ok = cok && (unsigned)(ih0[i] + dy) < (unsigned)a.h &&
+                        (unsigned)(iw0[i] + dx) < (unsigned)a.w;
+        const float* src = ok ? a.x + (roff[i] + koff) : a.x;
+        const uint32_t dst = sbase + row * 64 + ((lchunk ^ ((row >> 1) & 3)) << 4);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+                     "r"(ok ? 16 : 0)
+                     : "memory");
+      }
+      if (++pcb == a.cb) {
+        pcb = 0;
+        if (++pks == a.s) {
+          pks = 0;
+          if (++pkr == a.r) {
+            pkr = 0;
+            ptile += gridDim.x;
+            if (ptile < a.tiles) setup_rows();
+          }
         }
-      };
-      fetch(0, nxt);
-      for (int kb = 0; kb < KB; ++kb, ++g) {
-        float4 cur[TC_A_ROWS];
+      }
+    };
+    if (total > 0) setup_rows();
 #pragma unroll
-        for (int i = 0; i < TC_A_ROWS; ++i) cur[i] = nxt[i];
-        if (kb + 1 < KB) fetch(kb + 1, nxt);  // next loads in flight while storing this block
-        const int st = (int)(g % S);
-        if (!mbar_wait(&empty[st], (uint32_t)((g / S) & 1) ^ 1u, TC_ERR_WAIT_EMPTY)) {
-          alive = false;
-          break;
-        }
-        uint8_t* ahi = smem + (size_t)st * stage_bytes;
-        uint8_t* alo = ahi + a_bytes;
+    for (int d = 0; d < TC_STG_DEPTH; ++d) {
+      if (d < total) prefetch(d);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    int st = 0;
+    uint32_t par = 0;
+    for (int64_t g = 0; g < total; ++g) {
+      const int slot = (int)(g & (TC_STG_DEPTH - 1));
+      asm volatile("cp.async.wait_group %0;" ::"n"(TC_STG_DEPTH - 1) : "memory");
+      __syncwarp();
+      float hi[16], lo[16];
 #pragma unroll
-        for (int i = 0; i < TC_A_ROWS; ++i) {
-          const uint32_t off = (uint32_t)(row0 + 32 * i) * 128u + swz;
-          const float4 hv = split_hi(cur[i]);
-          *reinterpret_cast<float4*>(ahi + off) = hv;
-          *reinterpret_cast<float4*>(alo + off) =
-              make_float4(cur[i].x - hv.x, cur[i].y - hv.y, cur[i].z - hv.z, cur[i].w - hv.w);
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&full_a[st]);
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float4 v;
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                     : "r"(stg + slot * TC_STG_SLOT + lane * 64 + ((c4 ^ ((lane >> 1) & 3)) << 4)));
+        const float4 hv = split_hi(v);
+        hi[4 * c4 + 0] = hv.x; hi[4 * c4 + 1] = hv.y; hi[4 * c4 + 2] = hv.z; hi[4 * c4 + 3] = hv.w;
+        lo[4 * c4 + 0] = v.x - hv.x; lo[4 * c4 + 1] = v.y - hv.y;
+        lo[4 * c4 + 2] = v.z - hv.z; lo[4 * c4 + 3] = v.w - hv.w;
+      }
+      __syncwarp();
+      if (g + TC_STG_DEPTH < total) prefetch(slot);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      if (!mbar_wait(&empty[st], par ^ 1u, TC_ERR_WAIT_EMPTY)) break;
+      const uint32_t col = (uint32_t)(st * TC_A_COLS + half * 16);
+      tmem_st16(tm_rows + col, hi);
+      tmem_st16(tm_rows + col + 32, lo);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(&full_a[st]);
+      if (++st == S) {
+        st = 0;
+        par ^= 1u;
       }
     }
+    // No copy may land in shared memory after the CTA has exited.
+    asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == TC_WARP_TMA) {
     // ---------------- weights via TMA ----------------
     if (lane == 0) {
       int64_t g = 0;
+      int st = 0;
+      uint32_t par = 0;
       bool alive = true;
       for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x) {
         const int n0 = (int)(tile % a.n_tiles) * a.bn;
         for (int kb = 0; kb < KB; ++kb, ++g) {
-          const int st = (int)(g % S);
-          if (!mbar_wait(&empty[st], (uint32_t)((g / S) & 1) ^ 1u, TC_ERR_WAIT_EMPTY)) {
+          if (!mbar_wait(&empty[st], par ^ 1u, TC_ERR_WAIT_EMPTY)) {
             alive = false;
             break;
           }
-          uint8_t* bhi = smem + (size_t)st * stage_bytes + 2 * a_bytes;
+          uint8_t* bhi = smem + (size_t)st * L.stage_bytes;
           mbar_arrive_expect_tx(&full_b[st], 2 * b_bytes);
           tma_load_2d(bhi, &wmap_hi, &full_b[st], kb * TC_BK, n0);
           tma_load_2d(bhi + b_bytes, &wmap_lo, &full_b[st], kb * TC_BK, n0);
+          if (++st == S) {
+            st = 0;
+            par ^= 1u;
+          }
         }
       }
       // Bulk copies must not outlive the CTA's shared memory.
       for (int64_t k = (g > S ? g - S : 0); k < g; ++k)
         mbar_wait(&full_b[k % S], (uint32_t)((k / S) & 1), TC_ERR_WAIT_B);
     }
-  } else if (warp == TC_WARP_MMA) {
-    // ---------------- MMA issue: periods into two TMEM buffers ----------------
-    if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(TC_BM, a.bn);
-      int64_t g = 0, pc = 0;
-      bool alive = true;
-      for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x) {
-        for (int p = 0; p < NP && alive; ++p, ++pc) {
-          const int b = (int)(pc & 1);
-          if (!mbar_wait(&buf_free[b], (uint32_t)((pc >> 1) & 1) ^ 1u, TC_ERR_WAIT_ACC)) {
-            alive = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + (uint32_t)(b * a.bn);
-          const int kb_end = min(KB, (p + 1) * a.period);
-          for (int kb = p * a.period; kb < kb_end; ++kb, ++g) {
-            const int st = (int)(g % S);
-            const uint32_t par = (uint32_t)((g / S) & 1);
-            if (!mbar_wait(&full_a[st], par, TC_ERR_WAIT_A) ||
-                !mbar_wait(&full_b[st], par, TC_ERR_WAIT_B)) {
-              alive = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t ahi = smem_addr(smem + (size_t)st * stage_bytes);
-            const uint32_t alo = ahi + a_bytes;
-            const uint32_t bhi = alo + a_bytes;
-            const uint32_t blo = bhi + b_bytes;
-#pragma unroll
-            for (int k = 0; k < TC_BK / 8; ++k) {
-              const uint64_t dah = smem_desc_sw128(ahi + 32 * k), dal = smem_desc_sw128(alo + 32 * k);
-              const uint64_t dbh = smem_desc_sw128(bhi + 32 * k), dbl = smem_desc_sw128(blo + 32 * k);
-              mma_tf32(d, dah, dbh, idesc, (kb > p * a.period || k > 0) ? 1u : 0u);
-              mma_tf32(d, dah, dbl, idesc, 1u);
-              mma_tf32(d, dal, dbh, idesc, 1u);
-            }
-            mma_commit(&empty[st]);
-          }
-          mma_commit(&buf_full[b]);  // arrives once the period's MMAs have completed
-        }
-      }
-      if (!alive) {
-        // Error path: make sure no MMA still writes TMEM before it is freed.
-        mma_commit(drain);
-        mbar_wait(drain, 0u, TC_ERR_WAIT_ACC);
-      }
-    }
-  } else {
+  } else if (warp == TC_WARP_HH) {
+    if (lane == 0)
+      tc_issue<0>(a, smem, L, tmem, full_a, full_b, empty, hh_full, hh_free, cross_full, cross_free, drain);
+  } else if (warp == TC_WARP_HL) {
+    if (lane == 0)
+      tc_issue<1>(a, smem, L, tmem, full_a, full_b, empty, hh_full, hh_free, cross_full, cross_free, drain);
+  } else if (warp == TC_WARP_LH) {
+    if (lane == 0)
+      tc_issue<2>(a, smem, L, tmem, full_a, full_b, empty, hh_full, hh_free, cross_full, cross_free, drain);
+  } else if (warp >= TC_WARP_EPI) {
     // ---------------- promotion (fp32 RN adds) + epilogue ----------------
+    // Two warps per TMEM lane quarter; warp half h owns the 16-column chunks
+    // h, h + 2, h + 4 of the tile.  The fp32 total of a tile lives in
+    // registers (one output row per thread), indexed with compile-time
+    // offsets only.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int h = (warp - TC_WARP_EPI) >> 2;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    const uint32_t total = lane_base + (uint32_t)(2 * a.bn);
-    int64_t pc = 0;
+    const int nchunk = a.bn >> 4;
+    int64_t pc = 0, tc = 0;
     bool alive = true;
-    for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x) {
-      const int64_t m0 = (tile / a.n_tiles) * TC_BM;
-      const int n0 = (int)(tile % a.n_tiles) * a.bn;
-      const int64_t m = m0 + q * 32 + lane;
-      const bool rv = m < a.m_total;
-      int64_t ybase = 0, rbase = 0;
-      if (rv) {
-        const int ow_ = (int)(m % a.ow);
-        const int64_t qq = m / a.ow;
-        const int oh_ = (int)(qq % a.oh);
-        const int64_t n_ = qq / a.oh;
-        ybase = n_ * a.ys0 + (int64_t)oh_ * a.ys2 + (int64_t)ow_ * a.ys3;
-        rbase = n_ * a.rs0 + (int64_t)oh_ * a.rs2 + (int64_t)ow_ * a.rs3;
-      }
+    for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x, ++tc) {
+      float tot[TC_EPI_CHUNKS * 16];
       for (int p = 0; p < NP; ++p, ++pc) {
         const int b = (int)(pc & 1);
-        if (!mbar_wait(&buf_full[b], (uint32_t)((pc >> 1) & 1), TC_ERR_WAIT_ACC)) {
+        if (!mbar_wait(&hh_full[b], (uint32_t)((pc >> 1) & 1), TC_ERR_WAIT_ACC)) {
           alive = false;
           break;
         }
         tc_fence_after();
-        const bool last = p == NP - 1;
-        const uint32_t buf = lane_base + (uint32_t)(b * a.bn);
-        for (int c0 = 0; c0 < a.bn; c0 += 16) {
-          float v[16];
-          tmem_ld16(buf + (uint32_t)c0, v);
-          if (p > 0) {
-            float tv[16];
-            tmem_ld16(total + (uint32_t)c0, tv);
+        const uint32_t buf = lane_base + acc0 + (uint32_t)(b * a.bn);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = __fadd_rn(v[e], tv[e]);
-          }
-          if (!last) {
-            tmem_st16(total + (uint32_t)c0, v);
-            continue;
-          }
-          if (!rv || g_tc_error != 0) continue;
+        for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
+          const int c = h + 2 * j;
+          if (c < nchunk) {
+            uint32_t v[16];
+            tmem_ld16_nowait(buf + (uint32_t)(16 * c), v);
+            tmem_wait_ld();
 #pragma unroll
-          for (int gq = 0; gq < 4; ++gq) {
-            const int ch = n0 + c0 + 4 * gq;
-            if (ch >= a.kout) break;
-            float o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int cc = ch + e;
-              float val = v[4 * gq + e];
-              if (cc < a.kout) {
-                if (a.bias) val += a.bias[cc];
-                if (a.res && a.res_before_act) val += a.res[rbase + cc];
-                val = tc_act(val, a.act);
-                if (a.res && !a.res_before_act) val += a.res[rbase + cc];
-              }
-              o[e] = val;
-            }
-            if (a.vec_store && ch + 3 < a.kout) {
-              *reinterpret_cast<float4*>(a.y + ybase + ch) = make_float4(o[0], o[1], o[2], o[3]);
-            } else {
-              for (int e = 0; e < 4 && ch + e < a.kout; ++e) a.y[ybase + ch + e] = o[e];
-            }
+            for (int e = 0; e < 16; ++e)
+              tot[16 * j + e] = p == 0 ? __uint_as_float(v[e]) : __fadd_rn(tot[16 * j + e], __uint_as_float(v[e]));
           }
         }
-        if (!last) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
-        mbar_arrive(&buf_free[b]);
+        mbar_arrive(&hh_free[b]);
+      }
+      if (!alive) break;
+      if (!mbar_wait(cross_full, (uint32_t)(tc & 1), TC_ERR_WAIT_ACC)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t cross = lane_base + acc0 + (uint32_t)(2 * a.bn);
+#pragma unroll
+      for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
+        const int c = h + 2 * j;
+        if (c < nchunk) {
+          uint32_t u[16], w[16];
+          tmem_ld16_nowait(cross + (uint32_t)(16 * c), u);
+          tmem_ld16_nowait(cross + (uint32_t)(a.bn + 16 * c), w);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            tot[16 * j + e] =
+                __fadd_rn(tot[16 * j + e], __fadd_rn(__uint_as_float(u[e]), __uint_as_float(w[e])));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(cross_free);
+      if (g_tc_error != 0) continue;
+
+      const int m0 = (int)(tile / a.n_tiles) * TC_BM;
+      const int n0 = (int)(tile % a.n_tiles) * a.bn;
+      const int m = m0 + q * 32 + lane;
+      if (m >= a.m_total) continue;
+      const unsigned ow_ = (unsigned)m % (unsigned)a.ow;
+      const unsigned qq = (unsigned)m / (unsigned)a.ow;
+      const unsigned oh_ = qq % (unsigned)a.oh;
+      const unsigned n_ = qq / (unsigned)a.oh;
+      float* yrow = a.y + ((int64_t)n_ * a.ys0 + (int64_t)oh_ * a.ys2 + (int64_t)ow_ * a.ys3);
+      const float* rrow =
+          a.res ? a.res + ((int64_t)n_ * a.rs0 + (int64_t)oh_ * a.rs2 + (int64_t)ow_ * a.rs3) : nullptr;
+      // Bias comes from shared memory and the residual through the read-only
+      // path, so no global load has to wait behind a store that might alias it.
+#pragma unroll
+      for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
+        const int c = h + 2 * j;
+        const int cb0 = n0 + 16 * c;
+        if (c >= nchunk || cb0 >= a.kout) break;
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+          const int c4 = cb0 + 4 * v4;
+          if (c4 >= a.kout) break;
+          const bool full = c4 + 4 <= a.kout;
+          float rv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (rrow) {
+            if (a.res_vec && full) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(rrow + c4));
+              rv[0] = t.x; rv[1] = t.y; rv[2] = t.z; rv[3] = t.w;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) rv[e] = c4 + e < a.kout ? __ldg(rrow + c4 + e) : 0.f;
+            }
+          }
+          float o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float val = tot[16 * j + 4 * v4 + e];
+            if (a.bias) val += bias_s[min(c4 + e, a.kout - 1)];
+            if (rrow && a.res_before_act) val += rv[e];
+            val = tc_act(val, a.act);
+            if (rrow && !a.res_before_act) val += rv[e];
+            o[e] = val;
+          }
+          if (a.vec_store && full) {
+            *reinterpret_cast<float4*>(yrow + c4) = make_float4(o[0], o[1], o[2], o[3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (c4 + e < a.kout) yrow[c4 + e] = o[e];
+          }
+        }
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == TC_WARP_MMA) {
+  if (warp == TC_WARP_HH) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(a.tmem_cols)
+                 "r"(TC_TMEM_COLS)
                  : "memory");
   }
 }
@@ -647,12 +856,14 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   a.oh = (int)oh; a.ow = (int)ow; a.kout = k_out;
   a.r = r; a.s = s; a.sh = p->stride_h; a.sw = p->stride_w; a.ph = p->pad_h; a.pw = p->pad_w;
   a.dh = p->dil_h; a.dw = p->dil_w;
-  a.m_total = m_total;
+  if (m_total > 0x7fffffffLL - TC_BM) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: too many output pixels");
+  if (k_out > TC_MAX_BIAS) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: too many output channels");
+  a.m_total = (int)m_total;
   a.cb = c_pad / TC_BK;
   a.kb_total = r * s * a.cb;
-  // N tiles of at most 128 channels, balanced (e.g. 144 -> 2 x 80, 256 -> 2 x 128).
+  // N tiles of at most TC_MAX_BN channels, balanced (128 -> 2 x 64, 144 -> 2 x 80).
   {
-    const int ntiles = (k_out + 127) / 128;
+    const int ntiles = (k_out + TC_MAX_BN - 1) / TC_MAX_BN;
     const int per = (k_out + ntiles - 1) / ntiles;
     a.bn = ((per + 15) / 16) * 16;
   }
@@ -661,35 +872,56 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   a.act = p->act;
   a.res_before_act = p->residual_before_act;
   a.vec_store = nhwc_ok(y) ? 1 : 0;
-  // Two period buffers plus the fp32 total: 3 * bn columns (power of two >= 32).
-  uint32_t cols = 32;
-  while (cols < (uint32_t)(3 * a.bn)) cols <<= 1;
-  a.tmem_cols = cols;
-  const int64_t ktot = (int64_t)r * s * c_pad;
-  const size_t stage_bytes = 2 * (size_t)TC_BM * 128 + 2 * (size_t)a.bn * 128;
-  const size_t budget = 200 * 1024;
-  int stages = (int)((budget - 2048) / stage_bytes);
-  if (stages > 6) stages = 6;
-  if (stages < 2) stages = 2;
+  a.res_vec = residual && nhwc_ok(residual) ? 1 : 0;
+  // TMEM (512 columns): S A stages of 64 columns plus four accumulators of bn
+  // columns (two hi*hi period buffers, the hi*lo and lo*hi tile sums).
+  int stages = (int)((TC_TMEM_COLS - 4 * a.bn) / TC_A_COLS);
+  if (stages > TC_MAX_STAGES) stages = TC_MAX_STAGES;
+  if (stages < 2) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: N tile too wide for TMEM");
   a.stages = stages;
-  const size_t smem = 1024 + (size_t)stages * stage_bytes + (3 * stages + 5) * 8 + 16;
+  const int64_t ktot = (int64_t)r * s * c_pad;
+  size_t smem = TcSmem::make(a.bn, stages, k_out).bytes();
 
   CUtensorMap mhi, mlo;
   if ((rc = weight_map(w_hi, ktot, k_pad, a.bn, &mhi)) != MM_OK) return rc;
   if ((rc = weight_map(w_lo, ktot, k_pad, a.bn, &mlo)) != MM_OK) return rc;
 
-  static thread_local size_t configured = 0;
-  if (configured < smem) {
-    MM_CUDA(cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem),
-            "mm_conv2d_tc: shared memory attribute");
-    configured = smem;
+  // The kernel owns all 512 TMEM columns, so a second resident CTA on an SM
+  // would stall in tcgen05.alloc until the first exits: pad the shared-memory
+  // request whenever the occupancy calculator allows more than one CTA.
+  int dev = 0;
+  MM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  {
+    static size_t configured[256] = {};
+    static size_t min_smem[256] = {};
+    std::lock_guard<std::mutex> g(g_map_mu);
+    if (dev < 0 || dev >= 256) return fail(MM_ERR_INVALID, "mm_conv2d_tc: device index");
+    if (configured[dev] == 0) {
+      const size_t full = 200 * 1024;
+      MM_CUDA(cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)full),
+              "mm_conv2d_tc: shared memory attribute");
+      configured[dev] = full;
+      size_t lo = 16 * 1024;
+      for (size_t req = lo; req <= full; req += 4096) {
+        int blocks = 0;
+        MM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, conv_tc_kernel, TC_THREADS, req),
+                "mm_conv2d_tc: occupancy");
+        if (blocks <= 1) {
+          min_smem[dev] = req;
+          break;
+        }
+      }
+      if (min_smem[dev] == 0) min_smem[dev] = full;
+    }
+    if (smem < min_smem[dev]) smem = min_smem[dev];
+    if (smem > configured[dev]) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: shared memory");
   }
   const int64_t mt = (m_total + TC_BM - 1) / TC_BM;
   a.tiles = mt * a.n_tiles;
-  // Persistent CTAs: one per SM (the shared-memory footprint allows one).
+  // Persistent CTAs: one per SM.
   const int64_t ctas = a.tiles < (int64_t)sm_count() ? a.tiles : (int64_t)sm_count();
-  conv_tc_kernel<<<(unsigned)ctas, TC_V2_THREADS, smem, resolve_stream(stream)>>>(mhi, mlo, a);
+  conv_tc_kernel<<<(unsigned)ctas, TC_THREADS, smem, resolve_stream(stream)>>>(mhi, mlo, a);
   MM_LAUNCH_CHECK("mm_conv2d_tc launch");
   return MM_OK;
 }
