@@ -311,7 +311,12 @@ class PreparedConv2d(nn.Module):
 
 
 class PreparedLinear(nn.Module):
-    """Linear (+ ReLU/SiLU) as one GEMM with a fused epilogue."""
+    """Linear (+ ReLU/SiLU) as one GEMM with a fused epilogue.
+
+    The GEMM runs on the tcgen05 3xTF32 kernel as a 1x1 convolution over the
+    [M, K] row-major activation (one "pixel" per row) when K % 4 == 0 and the
+    rows are 16-byte aligned; otherwise on the SIMT GEMM (reference semantics
+    of addmm: backends/opengl/ops/matmul.py:262-281)."""
 
     def __init__(self, linear: nn.Linear, act: int = _lib.ACT_NONE, source=None):
         super().__init__()
@@ -324,26 +329,66 @@ class PreparedLinear(nn.Module):
         self._device_weights: dict[int, tuple] = {}
         _copy_routing_attrs(self, source)
 
+    @property
+    def tc_eligible(self) -> bool:
+        return self.in_features % 4 == 0
+
+    def tc_planes(self) -> tuple[torch.Tensor, torch.Tensor, int, int]:
+        """[N_pad, K_pad] tf32 high part and fp32 remainder of W (zero padded)."""
+        n, k = self.out_features, self.in_features
+        k_pad = (k + 31) // 32 * 32
+        n_pad = (n + 15) // 16 * 16
+        packed = torch.zeros(n_pad, k_pad, dtype=torch.float32)
+        packed[:n, :k] = self.weight_kn.t()
+        hi = tf32_round_nearest(packed)
+        return hi.contiguous(), (packed - hi).contiguous(), k_pad, n_pad
+
     def device_weights(self, rt):
         entry = self._device_weights.get(rt.index)
         if entry is None:
             ws = rt.upload(self.weight_kn, kind=_lib.POOL_PARAMETER, sync=True)
             bs = rt.upload(self.bias, kind=_lib.POOL_PARAMETER, sync=True)
+            tc = None
+            if self.tc_eligible:
+                hi, lo, k_pad, n_pad = self.tc_planes()
+                hs = rt.upload(hi, kind=_lib.POOL_PARAMETER, sync=True)
+                ls = rt.upload(lo, kind=_lib.POOL_PARAMETER, sync=True)
+                tc = (MatrixManTensor(hs, tuple(hi.shape), 0, (hi.shape[1], 1)),
+                      MatrixManTensor(ls, tuple(lo.shape), 0, (lo.shape[1], 1)), k_pad, n_pad)
             entry = (MatrixManTensor(ws, tuple(self.weight_kn.shape), 0,
                                      contiguous_strides(tuple(self.weight_kn.shape))),
-                     MatrixManTensor(bs, (self.out_features,), 0, (1,)))
+                     MatrixManTensor(bs, (self.out_features,), 0, (1,)), tc)
             self._device_weights[rt.index] = entry
         return entry
+
+    def _gemm_tc(self, x2: MatrixManTensor, bias: MatrixManTensor, tc) -> MatrixManTensor | None:
+        m, k = (int(v) for v in x2.shape)
+        rs, cs = x2._logical_strides
+        if cs != 1:
+            return None
+        hi, lo, k_pad, n_pad = tc
+        n = self.out_features
+        out = ops.empty(x2.runtime, (m, n))
+        x4 = MatrixManTensor(x2._owner, (m, k, 1, 1), x2._storage_offset, (rs, 1, rs, rs))
+        y4 = MatrixManTensor(out._owner, (m, n, 1, 1), out._storage_offset, (n, 1, n, n))
+        if ops.conv_tc(x4, hi, lo, n, k, 1, 1, k_pad, n_pad, bias, (1, 1), (0, 0), (1, 1), self.act,
+                       None, False, y4):
+            return out
+        return None
 
     def forward(self, x):
         if not isinstance(x, MatrixManTensor):
             raise RuntimeError("PreparedLinear requires a MatrixMan CUDA tensor")
-        w, b = self.device_weights(x.runtime)
+        w, b, tc = self.device_weights(x.runtime)
         lead = tuple(int(v) for v in x.shape[:-1])
         x2 = x
         if x.dim() != 2:
             x2 = x.reshape(-1, self.in_features)
-        y = ops.gemm(x2, w, b, act=self.act)
+        y = None
+        if tc is not None and config.convAlgo != "simt" and not config.cudaDisableSpecializedConv:
+            y = self._gemm_tc(x2, b, tc)
+        if y is None:
+            y = ops.gemm(x2, w, b, act=self.act)
         if x.dim() != 2:
             y = y.view(*lead, self.out_features)
         return y

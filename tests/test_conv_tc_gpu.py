@@ -113,6 +113,67 @@ def test_tc_matches_simt_path(mm):
     assert max_rel_err(y_tc, y_simt) < 1e-5
 
 
+def test_tc_deep_reduction_unbiased(mm):
+    """All-positive data is the worst case for the tensor core's truncating
+    accumulation (every partial sum moves away from zero).  With period
+    promotion the error stays at fp32 rounding level over 144 k-blocks."""
+    g = gen(21)
+    c, k = 512, 64
+    conv = nn.Conv2d(c, k, 3, 1, 1, bias=False)
+    with torch.no_grad():
+        conv.weight.copy_(torch.rand(conv.weight.shape, generator=g) / (c * 9))
+    unit = PreparedConv2d(conv, 0)
+    x = torch.rand(1, c, 12, 12, generator=g)
+    ref = O.conv2d(x, conv.weight.detach(), None, 1, 1)
+    y = unit(nhwc(mm, x)).cpu()
+    err = max_rel_err(y, ref)
+    assert err < 5e-6, f"max relative error {err:.3g}"
+    # no systematic drift: mean signed relative deviation near zero
+    drift = ((y - ref) / ref.abs().clamp_min(1e-30)).mean().item()
+    assert abs(drift) < 1e-6, f"mean drift {drift:.3g}"
+
+
+@pytest.mark.parametrize("m,k,n,act", [
+    (256, 784, 512, 1),    # MLP layer 1 (K padded to 800)
+    (256, 256, 10, 0),     # MLP head: N not a multiple of 4 (scalar stores)
+    (32, 512, 1000, 0),    # ResNet-18 fc: 13 N tiles
+    (1, 64, 48, 2),        # single row
+    (300, 128, 96, 0),     # ragged M (3 tiles, last partial)
+])
+def test_tc_linear(mm, m, k, n, act):
+    from matrixman_b200 import telemetry
+    from matrixman_b200.preparation import PreparedLinear
+    g = gen(m + k + n)
+    lin = nn.Linear(k, n)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(n, k, generator=g) / k ** 0.5)
+        lin.bias.copy_(torch.randn(n, generator=g) * 0.1)
+    unit = PreparedLinear(lin, act)
+    assert unit.tc_eligible
+    x = torch.randn(m, k, generator=g)
+    ref = ACTS[act](O.addmm(lin.bias.detach(), x, lin.weight.detach().t()))
+    before = telemetry.launches["mm_conv2d_tc"]
+    y = unit(mm.to_device(x))
+    assert telemetry.launches["mm_conv2d_tc"] == before + 1, "tensor-core GEMM did not run"
+    err = max_rel_err(y.cpu(), ref)
+    assert err < 1e-5, f"max relative error {err:.3g}"
+
+
+def test_tc_linear_unaligned_rows_fall_back(mm):
+    """K % 4 != 0 cannot be read with 16-byte copies: the SIMT GEMM runs."""
+    from matrixman_b200 import telemetry
+    from matrixman_b200.preparation import PreparedLinear
+    g = gen(3)
+    lin = nn.Linear(30, 7)
+    unit = PreparedLinear(lin, 0)
+    assert not unit.tc_eligible
+    x = torch.randn(5, 30, generator=g)
+    before = telemetry.launches["mm_conv2d_tc"]
+    y = unit(mm.to_device(x)).cpu()
+    assert telemetry.launches["mm_conv2d_tc"] == before
+    assert max_rel_err(y, O.addmm(lin.bias.detach(), x, lin.weight.detach().t())) < CONV_GEMM_REL
+
+
 def test_no_kernel_error_recorded(mm):
     import ctypes
     code = ctypes.c_int(-1)
