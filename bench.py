@@ -41,12 +41,14 @@ ANCHORS = (IMAGE // 8) ** 2 + (IMAGE // 16) ** 2 + (IMAGE // 32) ** 2
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--batch", type=int, default=BATCH)
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile-case", action="store_true",
+                   help="run --steps eager forwards (no graphs, no timing) for an ncu capture")
     return p.parse_args()
 
 
@@ -75,7 +77,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -162,7 +164,7 @@ def cpu_baseline(model, batch_sample: int, min_seconds: float = 12.0) -> dict:
             model(x)
             n += 1
             el = time.perf_counter() - t0
-            if el >= min_seconds or n >= 50:
+            if el >= min_seconds or n >= 200:
                 break
     return {"value": n * batch_sample / el, "unit": UNIT, "cores": torch.get_num_threads(),
             "kind": "port",
@@ -178,6 +180,7 @@ def run_b200(args):
     import workloads as W
     from matrixman_b200 import runtime
     from matrixman_b200 import telemetry as profiling
+    from matrixman_b200.replicas import gather_to_root
     from workloads.yolov8 import macs_per_image
 
     world, rank, local = dist_env()
@@ -199,24 +202,41 @@ def run_b200(args):
             dist.barrier()
         rt.synchronize()
 
+    sizes = [batch] * world
+
+    def step(xd):
+        """One step: the replica's forward; with several ranks, plus the
+        gather of every rank's [B, 84, 8400] output on rank 0 (NCCL over
+        NVLink, point to point)."""
+        y = prepared(xd)
+        if world > 1:
+            y = gather_to_root(y, sizes)
+        return y
+
     with torch.no_grad():
         for _ in range(max(args.warmup, 3)):
-            y = prepared(x_dev)
+            y = step(x_dev)
         del y
         barrier()
         clocks = ClockSampler(local)
         clocks.start()
+        # untimed pre-roll so the clock sampler is up before the timed region
+        t_pre = time.perf_counter()
+        while time.perf_counter() - t_pre < 0.4:
+            y = step(x_dev)
+            rt.synchronize()
         timer = runtime.Timer(rt)
         launches0 = profiling.total_launches()
         barrier()
         timer.start()
         for _ in range(args.steps):
-            y = prepared(x_dev)
+            y = step(x_dev)
         timer.stop()
         ms_total = timer.elapsed_ms()
         launch_calls = profiling.total_launches() - launches0
         barrier()
         clock_info = clocks.stop()
+        del y
     ms_step = ms_total / args.steps
     if world > 1:
         t = torch.tensor([ms_step], device="cuda")
@@ -224,26 +244,33 @@ def run_b200(args):
         ms_step = float(t.item())
     value = world * batch / (ms_step / 1e3)
 
-    # End to end: pinned host input -> public API -> .cpu() of the result.
+    # End to end: pinned host input -> public API -> .cpu() of the (gathered)
+    # result on rank 0.
     e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
     x_pinned = matrixman.pinned_empty(x_host.shape)
     x_pinned.copy_(x_host)
+
+    def e2e_step():
+        y = step(matrixman.to_device(x_pinned, device=local))
+        return y.cpu() if y is not None else None
+
     with torch.no_grad():
         for _ in range(2):
-            prepared(matrixman.to_device(x_pinned, device=local)).cpu()
+            out = e2e_step()
         barrier()
         t0 = time.perf_counter()
         for _ in range(e2e_steps):
-            out = prepared(matrixman.to_device(x_pinned, device=local)).cpu()
+            out = e2e_step()
         barrier()
         e2e_s = (time.perf_counter() - t0) / e2e_steps
     if world > 1:
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
+    out_numel = batch * (4 + NC) * ANCHORS * world
     e2e = {"value": world * batch / e2e_s, "unit": UNIT,
-           "h2d_bytes_per_step": int(x_host.numel() * 4),
-           "d2h_bytes_per_step": int(out.numel() * 4), "ms_per_step": e2e_s * 1e3}
+           "h2d_bytes_per_step": int(x_host.numel() * 4) * world,
+           "d2h_bytes_per_step": int(out_numel * 4), "ms_per_step": e2e_s * 1e3}
     return {"world": world, "rank": rank, "local": local, "value": value, "ms_step": ms_step,
             "clocks": clock_info, "e2e": e2e, "launch_calls": launch_calls, "prepared": prepared,
             "x_dev": x_dev, "model": model, "macs": macs_per_image(model), "batch": batch,
@@ -251,6 +278,23 @@ def run_b200(args):
 
 
 CONV_ENTRIES = ("mm_conv2d", "mm_conv2d_tc")
+TRAFFIC_SUMMARY = ROOT / "profiles" / "conv_tc_yolov8n_bs64_traffic.md"
+
+
+def conv_traffic_per_launch():
+    """DRAM bytes (read + write) per conv launch from the committed ncu summary
+    of one bs64 forward (line ``bytes_per_launch: N``), or None."""
+    if not TRAFFIC_SUMMARY.exists():
+        return None
+    for line in TRAFFIC_SUMMARY.read_text().splitlines():
+        if line.strip().startswith("bytes_per_launch:"):
+            try:
+                return {"bytes_per_launch": int(float(line.split(":", 1)[1].strip())),
+                        "source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                  f"{TRAFFIC_SUMMARY.relative_to(ROOT)}"}
+            except ValueError:
+                return None
+    return None
 
 
 def roofline(res: dict) -> tuple[dict, int, dict]:
@@ -268,14 +312,26 @@ def roofline(res: dict) -> tuple[dict, int, dict]:
     conv_launches = sum(summary[k]["launches"] for k in CONV_ENTRIES if k in summary)
     flops = 2.0 * res["macs"] * res["batch"]
     achieved = flops / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
-    peak = peaks["bf16_tflops"] / 2.0 / 3.0
+    # The conv kernels run back to back inside a long step: the sustained
+    # (power-capped) dense bf16 figure is the denominator.  fp32-accurate
+    # 3xTF32 issues three tf32 products (tf32 runs at half the bf16 rate) per
+    # algorithmic multiply-add, so its own ceiling is one sixth of that.
+    peak = peaks["bf16_tflops_sustained"]
+    ceiling = peak / 6.0
     kernels_per_forward = sum(v["launches"] for v in summary.values())
+    traffic = conv_traffic_per_launch()
     roof = {"bound": "tensor", "kernel": "+".join(k for k in CONV_ENTRIES if k in summary),
             "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
-            "frac": round(achieved / peak, 4) if peak else None, "traffic": None,
-            "peak_basis": f"{peaks['source']} bf16 {peaks['bf16_tflops']} TF/s / 2 (tf32) / 3 (3xTF32 split)",
+            "frac": round(achieved / peak, 4) if peak else None,
+            "traffic": traffic["bytes_per_launch"] if traffic else None,
+            "peak_basis": f"{peaks['source']} dense bf16, sustained ({peaks['bf16_tflops_sustained']} "
+                          f"TF/s; burst {peaks['bf16_tflops']})",
+            "ceiling_3xtf32": round(ceiling, 1), "frac_of_3xtf32_ceiling": round(achieved / ceiling, 4),
+            "tensor_issue_equiv_tflops": round(achieved * 6.0, 1),
             "launches_per_forward": conv_launches, "share_of_forward": round(conv_ms / total_ms, 3),
             "forward_ms_eager_events": round(total_ms, 3)}
+    if traffic:
+        roof["traffic_source"] = traffic["source"]
     shares = {k: {"launches": v["launches"], "ms": round(v["ms"], 4), "share": round(v["ms"] / total_ms, 4)}
               for k, v in sorted(summary.items(), key=lambda kv: -kv[1]["ms"])}
     return roof, kernels_per_forward, shares
@@ -286,6 +342,8 @@ def main():
     world, rank, local = dist_env()
     if args.impl == "reference":
         return run_reference(args, world, rank)
+    if args.profile_case:
+        return run_profile_case(args)
     res = run_b200(args)
     roof, kernels_per_forward, shares = roofline(res)
     line = {
@@ -294,7 +352,8 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic U[0,1] images, random-init weights (seeded)",
         "config": {"workload": f"yolov8n 640x640 fp32 inference, {res['batch']} images per GPU, "
-                               "prepared (BN folded, NHWC, CUDA graph)",
+                               "prepared (BN folded, NHWC, CUDA graph)"
+                               + (", outputs gathered on rank 0 (NCCL p2p)" if res["world"] > 1 else ""),
                    "batch_per_gpu": res["batch"], "global_batch": res["batch"] * res["world"],
                    "image": [IMAGE, IMAGE], "parallelism": f"replicas{res['world']}",
                    "l2": "inputs larger than L2 (315 MB input per step per GPU)"},
@@ -309,6 +368,25 @@ def main():
         res["dist"].destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def run_profile_case(args):
+    """Eager prepared forwards (no CUDA graph, no timing) for ncu launch lists:
+    one warm-up forward, then --steps forwards."""
+    import torch
+
+    import matrixman_b200 as matrixman
+    import workloads as W
+    matrixman.init()
+    matrixman.config.cuda_graphs = False
+    prepared = matrixman.prepare(W.yolov8_model("n"))
+    x = matrixman.to_device(W.yolo_input(args.batch, seed=1000))
+    with torch.no_grad():
+        prepared(x)
+        for _ in range(args.steps):
+            prepared(x)
+    matrixman.synchronize()
+    print(json.dumps({"profile_case": "yolov8n", "batch": args.batch, "forwards": args.steps + 1}))
 
 
 def run_reference(args, world, rank):

@@ -135,6 +135,9 @@ _FIELDS: dict[str, tuple] = {
                  "Convolution kernel: auto, simt (fp32 FFMA) or tc (tcgen05 3xTF32)."),
     "waitTimeoutMs": (600000, "MATRIXMAN_WAIT_TIMEOUT_MS", "wait_timeout_ms", "CUDA",
                       "backend-specific", "Bound on every host wait for device work."),
+    "readbackCacheMb": (2048, "MATRIXMAN_READBACK_CACHE_MB", "readback_cache_mb", "CUDA",
+                        "backend-specific",
+                        "Page-locked host memory kept for reuse by .cpu() results (0 = off)."),
 }
 
 _BOOL_FIELDS = {f for f, spec in _FIELDS.items() if isinstance(spec[0], bool) and f != "profile"}
@@ -225,6 +228,11 @@ def parse_value(field: str, value: Any) -> Any:
         number = int(value)
         if number <= 0:
             raise ValueError("waitTimeoutMs must be positive")
+        return number
+    if field == "readbackCacheMb":
+        number = int(value)
+        if number < 0:
+            raise ValueError("readbackCacheMb must be non-negative")
         return number
     if field == "tileSync":
         return _choice("tileSync", value, _TILE_SYNCS, "per_tile")

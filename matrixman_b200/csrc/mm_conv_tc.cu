@@ -13,7 +13,7 @@
 //     the exact fp32 remainder, and write both planes into a TMEM A stage with
 //     tcgen05.st -- so the MMAs read only the weights from shared memory;
 //   * warp 8 (TMA): prepacked [K_pad][R*S*C_pad] weight hi/lo planes, one 2-D
-//     tiled load each per stage (no multicast);
+//     tiled load each per stage into this CTA's shared memory;
 //   * warps 9, 10, 11 (MMA issue, one thread each): A_hi*B_hi, A_hi*B_lo and
 //     A_lo*B_hi, four tcgen05.mma.kind::tf32 per k-block each, into separate
 //     TMEM accumulators.  Three issuing threads overlap the per-instruction

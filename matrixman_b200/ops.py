@@ -17,7 +17,7 @@ import torch
 from . import _lib
 from . import telemetry as profiling
 from .config import config
-from .runtime import DeviceRuntime, get_runtime
+from .runtime import DeviceRuntime, activate_stream, get_runtime
 from .tensor import (
     MatrixManTensor,
     broadcast_shapes,
@@ -79,6 +79,7 @@ def empty_like(t: MatrixManTensor, shape=None) -> MatrixManTensor:
 
 def _launch(name: str, *args) -> None:
     lib = _lib_handle()
+    activate_stream(args[-1])
     token = profiling.launch_times.begin(name, args[-1]) if profiling.gpu_timing_enabled() else None
     status = getattr(lib, name)(*args)
     if status != _lib.MM_OK:
@@ -408,6 +409,7 @@ def conv_tc(x: MatrixManTensor, w_hi: MatrixManTensor, w_lo: MatrixManTensor, k_
     name = "mm_conv2d_tc"
     lib = _lib_handle()
     stream = x.runtime.stream
+    activate_stream(stream)
     token = profiling.launch_times.begin(name, stream) if profiling.gpu_timing_enabled() else None
     status = lib.mm_conv2d_tc(_p(x.desc()), ctypes.c_void_p(w_hi.element_ptr),
                               ctypes.c_void_p(w_lo.element_ptr), int(k_out), int(c_in), int(r), int(s),

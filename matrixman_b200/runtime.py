@@ -60,6 +60,22 @@ def set_device(index: int) -> None:
     _current_device.index = int(index)
     if index in _runtimes:
         _lib.call("mm_set_device", int(index))
+        _active_device.index = int(index)
+
+
+# Stream -> device of every initialised runtime; launches make the stream's
+# device current before enqueuing, so tensors of several devices can be used
+# from one thread (whole-model replicas).
+_stream_device: dict[int, int] = {}
+_active_device = threading.local()
+
+
+def activate_stream(stream) -> None:
+    """Make the CUDA device that owns `stream` current on this thread."""
+    dev = _stream_device.get(stream)
+    if dev is not None and getattr(_active_device, "index", -1) != dev:
+        _lib.call("mm_set_device", dev)
+        _active_device.index = dev
 
 
 def get_runtime(index: int | None = None) -> "DeviceRuntime":
@@ -150,6 +166,8 @@ class DeviceRuntime:
         s = ctypes.c_void_p()
         _lib.check(lib.mm_runtime_stream(self.index, ctypes.byref(s)), "runtime stream")
         self.stream = s.value
+        _stream_device[self.stream] = self.index
+        _active_device.index = -1  # mm_init may have changed the current device
         info = _lib.MMDeviceInfo()
         _lib.check(lib.mm_device_info(self.index, ctypes.byref(info)), "device info")
         self.info = {
@@ -328,6 +346,84 @@ class CudaGraph:
 
     def destroy(self) -> None:
         self._finalizer()
+
+
+class PinnedHostPool:
+    """Page-locked host blocks for readback results, reused across calls.
+
+    ``.cpu()`` returns ordinary CPU tensors; backing them with cached
+    page-locked blocks lets the copy engine write them at full link speed (no
+    driver bounce buffer, no first-touch page faults on a fresh allocation).
+    A block returns to the cache when the last tensor or view over it is
+    freed; at most ``config.readbackCacheMb`` stays cached, the rest is freed.
+    """
+
+    GRANULE = 1 << 21
+
+    def __init__(self):
+        self._free: dict[int, list[int]] = {}
+        self._cached = 0
+        self._lock = threading.Lock()
+
+    def empty(self, shape, dtype: torch.dtype) -> torch.Tensor | None:
+        cap = int(config.readbackCacheMb) << 20
+        n = 1
+        for v in shape:
+            n *= int(v)
+        nbytes = max(n, 1) * ELEMENT_SIZE[dtype]
+        size = (nbytes + self.GRANULE - 1) // self.GRANULE * self.GRANULE
+        if cap == 0 or size > cap:
+            return None
+        lib = _lib.load()
+        ptr = None
+        with self._lock:
+            blocks = self._free.get(size)
+            if blocks:
+                ptr = blocks.pop()
+                self._cached -= size
+        if ptr is None:
+            out = ctypes.c_void_p()
+            if lib.mm_host_alloc_pinned(size, ctypes.byref(out)) != _lib.MM_OK or not out.value:
+                return None
+            ptr = int(out.value)
+        buf = (ctypes.c_uint8 * size).from_address(ptr)
+        t = torch.frombuffer(buf, dtype=dtype, count=max(n, 1))[:n].view(tuple(int(v) for v in shape))
+        weakref.finalize(buf, self._release, ptr, size)
+        return t
+
+    def _release(self, ptr: int, size: int) -> None:
+        try:
+            cap = int(config.readbackCacheMb) << 20
+            with self._lock:
+                if self._cached + size <= cap:
+                    self._free.setdefault(size, []).append(ptr)
+                    self._cached += size
+                    return
+            _lib.load().mm_host_free_pinned(ctypes.c_void_p(ptr))
+        except Exception:
+            pass
+
+    def trim(self) -> None:
+        with self._lock:
+            blocks = [p for lst in self._free.values() for p in lst]
+            self._free.clear()
+            self._cached = 0
+        lib = _lib.load()
+        for p in blocks:
+            lib.mm_host_free_pinned(ctypes.c_void_p(p))
+
+    @property
+    def cached_bytes(self) -> int:
+        return self._cached
+
+
+pinned_pool = PinnedHostPool()
+
+
+def host_empty(shape, dtype: torch.dtype) -> torch.Tensor:
+    """CPU tensor for a readback: pooled page-locked memory when available."""
+    t = pinned_pool.empty(shape, dtype)
+    return t if t is not None else torch.empty(tuple(shape), dtype=dtype)
 
 
 class Timer:

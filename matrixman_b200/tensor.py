@@ -314,19 +314,20 @@ def readback_tensor(tensor: MatrixManTensor) -> torch.Tensor:
     n = numel(shape)
     if n == 0:
         return torch.empty(shape, dtype=tensor.dtype)
+    from .runtime import host_empty
     if is_contiguous(shape, strides):
-        out = torch.empty(shape, dtype=tensor.dtype)
+        out = host_empty(shape, tensor.dtype)
         rt.download(tensor.element_ptr, out)
         return out
     if is_dense(shape, strides):
         # Dense permutation (e.g. NHWC): copy the span, keep the strides.
-        flat = torch.empty(n, dtype=tensor.dtype)
+        flat = host_empty((n,), tensor.dtype)
         rt.download(tensor.element_ptr, flat)
         return torch.as_strided(flat, shape, strides)
     # Sliced / expanded views: gather on the device into a contiguous block.
     from . import ops
     dense = ops.materialize(tensor)
-    out = torch.empty(shape, dtype=tensor.dtype)
+    out = host_empty(shape, tensor.dtype)
     rt.download(dense.element_ptr, out)
     return out
 
