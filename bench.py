@@ -176,6 +176,15 @@ def run_b200(args):
     import torch
     import torch.distributed as dist
 
+    world, rank, local = dist_env()
+    if world > 1:
+        # The process group is created before the package registers its
+        # PrivateUse1 device, so torch's accelerator check sees CUDA.
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
     import matrixman_b200 as matrixman
     import workloads as W
     from matrixman_b200 import runtime
@@ -183,11 +192,6 @@ def run_b200(args):
     from matrixman_b200.replicas import gather_to_root
     from workloads.yolov8 import macs_per_image
 
-    world, rank, local = dist_env()
-    if world > 1:
-        torch.cuda.set_device(local)
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     runtime.set_device(local)
     matrixman.init()
     rt = runtime.get_runtime(local)
@@ -198,8 +202,12 @@ def run_b200(args):
     x_dev = matrixman.to_device(x_host, device=local)
 
     def barrier():
+        # an all-reduce of an explicit CUDA tensor (dist.barrier would place its
+        # tensor on the default accelerator, which is the matrixman device)
         if world > 1:
-            dist.barrier()
+            t = torch.zeros(1, device=torch.device("cuda", local))
+            dist.all_reduce(t)
+            torch.cuda.synchronize(local)
         rt.synchronize()
 
     sizes = [batch] * world
@@ -239,7 +247,7 @@ def run_b200(args):
         del y
     ms_step = ms_total / args.steps
     if world > 1:
-        t = torch.tensor([ms_step], device="cuda")
+        t = torch.tensor([ms_step], device=torch.device("cuda", local))
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_step = float(t.item())
     value = world * batch / (ms_step / 1e3)
@@ -264,7 +272,7 @@ def run_b200(args):
         barrier()
         e2e_s = (time.perf_counter() - t0) / e2e_steps
     if world > 1:
-        t = torch.tensor([e2e_s], device="cuda")
+        t = torch.tensor([e2e_s], device=torch.device("cuda", local))
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     out_numel = batch * (4 + NC) * ANCHORS * world
@@ -364,7 +372,10 @@ def main():
     if res["world"] == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(res["model"], 8)
     if res["dist"] is not None:
-        res["dist"].barrier()
+        import torch
+        t = torch.zeros(1, device=torch.device("cuda", res["local"]))
+        res["dist"].all_reduce(t)
+        torch.cuda.synchronize(res["local"])
         res["dist"].destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
