@@ -49,6 +49,9 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile-case", action="store_true",
                    help="run --steps eager forwards (no graphs, no timing) for an ncu capture")
+    p.add_argument("--profile-conv", default=None, metavar="C,K,KSIZE,STRIDE,HW",
+                   help="run one prepared convolution (SiLU epilogue) on a --batch x C x HW x HW "
+                        "NHWC input --steps + 1 times, for an ncu capture of one kernel")
     return p.parse_args()
 
 
@@ -352,6 +355,8 @@ def main():
         return run_reference(args, world, rank)
     if args.profile_case:
         return run_profile_case(args)
+    if args.profile_conv:
+        return run_profile_conv(args)
     res = run_b200(args)
     roof, kernels_per_forward, shares = roofline(res)
     line = {
@@ -398,6 +403,27 @@ def run_profile_case(args):
             prepared(x)
     matrixman.synchronize()
     print(json.dumps({"profile_case": "yolov8n", "batch": args.batch, "forwards": args.steps + 1}))
+
+
+def run_profile_conv(args):
+    import torch
+    from torch import nn
+
+    import matrixman_b200 as matrixman
+    from matrixman_b200.preparation import PreparedConv2d
+    c, k, ks, st, hw = (int(v) for v in args.profile_conv.split(","))
+    matrixman.init()
+    g = torch.Generator().manual_seed(7)
+    conv = nn.Conv2d(c, k, ks, st, ks // 2)
+    unit = PreparedConv2d(conv, 2)
+    x = torch.rand(args.batch, hw, hw, c, generator=g) * 2 - 1
+    xd = matrixman.to_device(x).permute(0, 3, 1, 2)
+    with torch.no_grad():
+        for _ in range(args.steps + 1):
+            y = unit(xd)
+    matrixman.synchronize()
+    print(json.dumps({"profile_conv": [c, k, ks, st, hw], "batch": args.batch,
+                      "launches": args.steps + 1, "out": list(y.shape)}))
 
 
 def run_reference(args, world, rank):

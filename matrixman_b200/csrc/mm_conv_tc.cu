@@ -77,6 +77,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about `ns` nanoseconds pass, instead of polling.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -96,12 +110,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1; i < TC_SPIN_LIMIT; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0) {
+    if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+    if ((i & 63) == 0) {
       if (tc_error_raised()) return false;
       if (global_ns() - t0 > TC_WAIT_NS) break;
     }
-    if (i > 64) __nanosleep(32);
   }
   atomicCAS(&g_tc_error, 0, code);
   return false;
@@ -190,10 +203,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Activation fused into the convolution epilogue.  Its result is judged with
+// the convolution's tolerance (max |diff| / max |ref| <= 1e-4), so the fast
+// exponential and division (a few ulp) are used here; the standalone
+// activation kernels keep correctly rounded arithmetic.  The exponent is
+// clamped so the denominator stays finite (x / (1 + e^88) is 0 to fp32).
 __device__ __forceinline__ float tc_act(float v, int act) {
   if (act == MM_ACT_RELU) return (v != v) ? v : (v > 0.f ? v : 0.f);
-  if (act == MM_ACT_SILU) return __fdiv_rn(v, 1.0f + expf(-v));
-  if (act == MM_ACT_SIGMOID) return __fdiv_rn(1.0f, 1.0f + expf(-v));
+  if (act == MM_ACT_SILU) return __fdividef(v, 1.0f + __expf(fminf(-v, 88.0f)));
+  if (act == MM_ACT_SIGMOID) return __fdividef(1.0f, 1.0f + __expf(fminf(-v, 88.0f)));
   return v;
 }
 

@@ -154,16 +154,15 @@ __global__ void copy_strided_kernel(const T* __restrict__ x, T* __restrict__ y, 
 
 // Copy of rows: y[r*ys + c] = x[r*xs + c] for c < cols, with cols % 4 == 0 and
 // 16-byte aligned rows (NHWC channel slices: cat / split materialisation).
+// One warp per row (grid-stride over rows), lanes stride over the row's
+// float4s: coalesced 16-byte accesses, no per-element index division.
 __global__ void copy_rows_vec4_kernel(const float* __restrict__ x, float* __restrict__ y,
-                                      int64_t rows, int64_t cols4, int64_t xs, int64_t ys) {
-  int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  int64_t nth = (int64_t)gridDim.x * blockDim.x;
-  int64_t total = rows * cols4;
-  for (int64_t i = tid; i < total; i += nth) {
-    int64_t r = i / cols4;
-    int64_t c = i - r * cols4;
-    float4 v = *reinterpret_cast<const float4*>(x + r * xs + c * 4);
-    *reinterpret_cast<float4*>(y + r * ys + c * 4) = v;
+                                      int64_t rows, int cols4, int64_t xs, int64_t ys) {
+  const int64_t wstride = (int64_t)gridDim.x * blockDim.y;
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.y + threadIdx.y; r < rows; r += wstride) {
+    const float4* src = reinterpret_cast<const float4*>(x + r * xs);
+    float4* dst = reinterpret_cast<float4*>(y + r * ys);
+    for (int c = threadIdx.x; c < cols4; c += 32) dst[c] = __ldg(src + c);
   }
 }
 
@@ -689,8 +688,38 @@ extern "C" int mm_arange(const mm_tensor_t* y, double start, double step, void* 
   return MM_OK;
 }
 
-static int copy_impl(const mm_tensor_t* x, const mm_tensor_t* y, cudaStream_t s) {
-  if (x->dtype != y->dtype) return fail(MM_ERR_UNSUPPORTED, "mm_copy: dtype mismatch");
+// Both operands with their dimensions reordered by the output's memory order
+// (largest stride first, ties keep logical order), so that channel slices of
+// channels-last buffers collapse to [pixels, channels] rows.
+static void memory_order(const mm_tensor_t* x, const mm_tensor_t* y, mm_tensor_t* xo,
+                         mm_tensor_t* yo) {
+  *xo = *x;
+  *yo = *y;
+  int perm[MM_MAX_DIMS];
+  for (int i = 0; i < y->ndim; ++i) perm[i] = i;
+  for (int i = 1; i < y->ndim; ++i) {  // insertion sort, stable
+    int p = perm[i], j = i - 1;
+    while (j >= 0 && y->stride[perm[j]] < y->stride[p]) {
+      perm[j + 1] = perm[j];
+      --j;
+    }
+    perm[j + 1] = p;
+  }
+  for (int i = 0; i < y->ndim; ++i) {
+    xo->size[i] = x->size[perm[i]];
+    xo->stride[i] = x->stride[perm[i]];
+    yo->size[i] = y->size[perm[i]];
+    yo->stride[i] = y->stride[perm[i]];
+  }
+}
+
+static int copy_impl(const mm_tensor_t* x_in, const mm_tensor_t* y_in, cudaStream_t s) {
+  if (x_in->dtype != y_in->dtype) return fail(MM_ERR_UNSUPPORTED, "mm_copy: dtype mismatch");
+  mm_tensor_t xo, yo;
+  if (x_in->ndim != y_in->ndim) return fail(MM_ERR_INVALID, "mm_copy: rank mismatch");
+  memory_order(x_in, y_in, &xo, &yo);
+  const mm_tensor_t* x = &xo;
+  const mm_tensor_t* y = &yo;
   const mm_tensor_t* ops[2] = {x, y};
   Geom g[2];
   int rc = collapse(2, ops, g);
@@ -707,11 +736,14 @@ static int copy_impl(const mm_tensor_t* x, const mm_tensor_t* y, cudaStream_t s)
   if (x->dtype == MM_F32 && g[0].nd == 2 && g[0].stride[1] == 1 && g[1].stride[1] == 1 &&
       g[0].size[1] % 4 == 0 && g[0].stride[0] % 4 == 0 && g[1].stride[0] % 4 == 0 &&
       ((((uintptr_t)x->data) | ((uintptr_t)y->data)) & 15) == 0) {
-    int64_t cols4 = g[0].size[1] / 4;
-    unsigned grid = grid_for(g[0].size[0] * cols4, 256, (int64_t)sm_count() * 8);
-    copy_rows_vec4_kernel<<<grid, 256, 0, s>>>((const float*)x->data, (float*)y->data,
-                                               g[0].size[0], cols4, g[0].stride[0],
-                                               g[1].stride[0]);
+    const int64_t rows = g[0].size[0];
+    const int64_t cols4 = g[0].size[1] / 4;
+    if (cols4 > 0x7fffffff) return fail(MM_ERR_UNSUPPORTED, "mm_copy: row too long");
+    int64_t blocks = (rows + 7) / 8;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    if (blocks > cap) blocks = cap;
+    copy_rows_vec4_kernel<<<(unsigned)blocks, dim3(32, 8), 0, s>>>(
+        (const float*)x->data, (float*)y->data, rows, (int)cols4, g[0].stride[0], g[1].stride[0]);
     MM_LAUNCH_CHECK("mm_copy launch");
     return MM_OK;
   }
