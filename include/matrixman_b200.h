@@ -121,7 +121,8 @@ typedef struct mm_conv_params {
   int32_t groups;
   int32_t act;                 /* mm_act_t applied in the epilogue */
   int32_t residual_before_act; /* 1: act(conv+bias+res); 0: act(conv+bias)+res */
-  int32_t algo;                /* 0 = auto, 1 = SIMT fp32, 2 = tcgen05 3xTF32 */
+  int32_t algo;                /* 0 = auto, 1 = SIMT fp32, 2 = tcgen05 3xTF32,
+                                  3 = implicit-GEMM SIMT only (no direct small-C kernel) */
 } mm_conv_params_t;
 
 /* ------------------------------------------------------------------------ */

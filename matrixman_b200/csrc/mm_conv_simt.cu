@@ -227,6 +227,130 @@ static int launch_conv(const ConvArgs& a, bool cfast, cudaStream_t s) {
   return MM_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Direct convolution for very few input channels (network stems: C_in = 3,
+// 3x3 or 7x7 taps).  The implicit-GEMM kernels would pad the reduction to a
+// full tile; here one thread computes one output pixel x 16 output channels
+// with FFMA, the [16][C][R][S] weight slice of its channel block sits in
+// shared memory (broadcast reads), and the 16 outputs leave as four float4
+// stores when the output is channels-last.  Bound: HBM (the input is read
+// about once through L1, the output written once).
+// ---------------------------------------------------------------------------
+
+constexpr int SC_KT = 16;  // output channels per thread
+
+__device__ __forceinline__ float act_fast(float v, int act) {
+  // Judged with the convolution tolerance, like the tensor-core epilogue.
+  if (act == MM_ACT_RELU) return (v != v) ? v : (v > 0.f ? v : 0.f);
+  if (act == MM_ACT_SILU) return __fdividef(v, 1.0f + __expf(fminf(-v, 88.0f)));
+  if (act == MM_ACT_SIGMOID) return __fdividef(1.0f, 1.0f + __expf(fminf(-v, 88.0f)));
+  return v;
+}
+
+template <int CIN, int R, int S>
+__global__ void __launch_bounds__(128) conv_smallc_kernel(ConvArgs a, int vec_store) {
+  __shared__ float4 wsm[CIN * R * S * (SC_KT / 4)];
+  const int k0 = blockIdx.y * SC_KT;
+  for (int i = threadIdx.x; i < CIN * R * S * SC_KT; i += blockDim.x) {
+    const int kk = i % SC_KT;
+    const int t = i / SC_KT;  // (c * R + r) * S + s
+    const int c = t / (R * S), rs = t - c * (R * S);
+    const int r = rs / S, s_ = rs - r * S;
+    const int k = k0 + kk;
+    reinterpret_cast<float*>(wsm)[i] =
+        k < a.kout ? a.w[k * a.ws[0] + c * a.ws[1] + r * a.ws[2] + s_ * a.ws[3]] : 0.f;
+  }
+  __syncthreads();
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < a.m_total; m += nthreads) {
+    const int ow_ = (int)(m % a.ow);
+    const int64_t q = m / a.ow;
+    const int oh_ = (int)(q % a.oh);
+    const int n_ = (int)(q / a.oh);
+    const int ih0 = oh_ * a.sh - a.ph, iw0 = ow_ * a.sw - a.pw;
+    const float* xb = a.x + (int64_t)n_ * a.xs[0];
+    float acc[SC_KT];
+#pragma unroll
+    for (int k = 0; k < SC_KT; ++k) acc[k] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CIN; ++c) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int ih = ih0 + r * a.dh;
+        const bool rok = (unsigned)ih < (unsigned)a.h;
+#pragma unroll
+        for (int s_ = 0; s_ < S; ++s_) {
+          const int iw = iw0 + s_ * a.dw;
+          const float v = (rok && (unsigned)iw < (unsigned)a.w_in)
+                              ? __ldg(xb + c * a.xs[1] + (int64_t)ih * a.xs[2] + (int64_t)iw * a.xs[3])
+                              : 0.f;
+          const float4* wp = wsm + ((c * R + r) * S + s_) * (SC_KT / 4);
+#pragma unroll
+          for (int k4 = 0; k4 < SC_KT / 4; ++k4) {
+            const float4 w4 = wp[k4];
+            acc[4 * k4 + 0] = fmaf(v, w4.x, acc[4 * k4 + 0]);
+            acc[4 * k4 + 1] = fmaf(v, w4.y, acc[4 * k4 + 1]);
+            acc[4 * k4 + 2] = fmaf(v, w4.z, acc[4 * k4 + 2]);
+            acc[4 * k4 + 3] = fmaf(v, w4.w, acc[4 * k4 + 3]);
+          }
+        }
+      }
+    }
+    const int64_t yb = (int64_t)n_ * a.ys[0] + (int64_t)oh_ * a.ys[2] + (int64_t)ow_ * a.ys[3];
+    const int64_t rb = (int64_t)n_ * a.rs[0] + (int64_t)oh_ * a.rs[2] + (int64_t)ow_ * a.rs[3];
+#pragma unroll
+    for (int k = 0; k < SC_KT; ++k) {
+      const int kk = min(k0 + k, a.kout - 1);
+      float v = acc[k];
+      if (a.bias) v += a.bias[kk];
+      if (a.res && a.res_before_act) v += a.res[rb + kk * a.rs[1]];
+      v = act_fast(v, a.act);
+      if (a.res && !a.res_before_act) v += a.res[rb + kk * a.rs[1]];
+      acc[k] = v;
+    }
+    if (vec_store && k0 + SC_KT <= a.kout) {
+      float4* yp = reinterpret_cast<float4*>(a.y + yb + k0);
+#pragma unroll
+      for (int k4 = 0; k4 < SC_KT / 4; ++k4)
+        yp[k4] = make_float4(acc[4 * k4], acc[4 * k4 + 1], acc[4 * k4 + 2], acc[4 * k4 + 3]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < SC_KT; ++k)
+        if (k0 + k < a.kout) a.y[yb + (int64_t)(k0 + k) * a.ys[1]] = acc[k];
+    }
+  }
+}
+
+template <int CIN, int R, int S>
+int launch_smallc(const ConvArgs& a, int vec_store, cudaStream_t s) {
+  const int64_t per_block = 128;
+  int64_t blocks = (a.m_total + per_block - 1) / per_block;
+  const int64_t cap = (int64_t)sm_count() * 16;
+  if (blocks > cap) blocks = cap;
+  dim3 grid((unsigned)blocks, (unsigned)((a.kout + SC_KT - 1) / SC_KT));
+  conv_smallc_kernel<CIN, R, S><<<grid, 128, 0, s>>>(a, vec_store);
+  MM_LAUNCH_CHECK("mm_conv2d small-channel launch");
+  return MM_OK;
+}
+
+// Returns MM_ERR_UNSUPPORTED when the geometry has no small-channel variant.
+int conv_smallc_dispatch(const ConvArgs& a, int vec_store, cudaStream_t s) {
+  if (a.groups != 1 || a.alpha != 1.f || a.c < 1 || a.c > 4 || a.kout > 65535 * SC_KT)
+    return MM_ERR_UNSUPPORTED;
+  const int rs = a.r * 16 + a.s;
+#define MM_SMALLC(C)                                              \
+  if (a.c == C) {                                                 \
+    if (rs == 3 * 16 + 3) return launch_smallc<C, 3, 3>(a, vec_store, s); \
+    if (rs == 7 * 16 + 7) return launch_smallc<C, 7, 7>(a, vec_store, s); \
+  }
+  MM_SMALLC(1)
+  MM_SMALLC(2)
+  MM_SMALLC(3)
+  MM_SMALLC(4)
+#undef MM_SMALLC
+  return MM_ERR_UNSUPPORTED;
+}
+
 int conv_simt_dispatch(const ConvArgs& a, bool cfast, cudaStream_t s) {
   if (a.kg <= 16) return launch_conv<128, 16, 16, 8, 2>(a, cfast, s);   // 128 threads
   if (a.kg <= 32) return launch_conv<128, 32, 16, 8, 4>(a, cfast, s);   // 128 threads
@@ -304,6 +428,12 @@ extern "C" int mm_conv2d(const mm_tensor_t* x, const mm_tensor_t* w, const float
   if (kt > 0x7fffffff) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d: reduction too large");
   a.k_total = (int)kt;
   if (a.m_total == 0 || a.kout == 0) return MM_OK;
+  if (p->algo != 3) {  // algo 3 forces the implicit-GEMM SIMT kernel (tests)
+    const bool vec = y->stride[1] == 1 && y->stride[0] % 4 == 0 && y->stride[2] % 4 == 0 &&
+                     y->stride[3] % 4 == 0 && (((uintptr_t)y->data) & 15) == 0;
+    const int rc2 = conv_smallc_dispatch(a, vec ? 1 : 0, resolve_stream(stream));
+    if (rc2 != MM_ERR_UNSUPPORTED) return rc2;
+  }
   // Channel-fastest K order when channels are the densest input dim (NHWC).
   bool cfast = x->stride[1] == 1 && a.c > 1;
   return conv_simt_dispatch(a, cfast, resolve_stream(stream));
