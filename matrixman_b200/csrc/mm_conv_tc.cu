@@ -223,8 +223,18 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
+// The same rounding with two integer operations: adding half a tf32 ulp to
+// the magnitude bits and clearing the 13 low mantissa bits rounds to nearest,
+// ties away from zero, for every finite value (the carry propagates into the
+// exponent exactly like a mantissa overflow).  Infinities and NaNs are not
+// preserved (an input that holds them makes the convolution non-finite
+// anyway).  Same formula as the host-side weight prepack.
+__device__ __forceinline__ float tf32_rna_int(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
 __device__ __forceinline__ float4 split_hi(float4 v) {
-  return make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+  return make_float4(tf32_rna_int(v.x), tf32_rna_int(v.y), tf32_rna_int(v.z), tf32_rna_int(v.w));
 }
 
 struct TcArgs {
@@ -491,7 +501,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int64_t ptile = blockIdx.x;
     int pkr = 0, pks = 0, pcb = 0;
     const int lane_c = half * 16 + lchunk * 4;
-    int64_t roff[4];
+    int roff[4];  // element offsets (the input spans < 2^31 elements; checked on the host)
     int ih0[4], iw0[4];
     auto setup_rows = [&]() {
       const int m0 = (int)(ptile / a.n_tiles) * TC_BM + q * 32;
@@ -506,8 +516,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // Rows past the end get a coordinate that fails the bounds test.
         ih0[i] = ok ? oh_ * a.sh - a.ph : -0x40000000;
         iw0[i] = ow_ * a.sw - a.pw;
-        roff[i] = (int64_t)(qq / (unsigned)a.oh) * a.xs0 + (int64_t)ih0[i] * a.xs2 +
-                  (int64_t)iw0[i] * a.xs3 + lane_c;
+        // Rows past the end keep an in-range base: their copies are zero-filled.
+        roff[i] = ok ? (int)((qq / (unsigned)a.oh) * (unsigned)a.xs0) + ih0[i] * (int)a.xs2 +
+                           iw0[i] * (int)a.xs3 + lane_c
+                     : 0;
       }
     };
     // Issue the copies of the cursor's k-block into `slot` and advance it.
@@ -515,14 +527,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int dy = pkr * a.dh, dx = pks * a.dw;
       const int cbase = pcb * TC_BK;
       const bool cok = cbase + lane_c < a.c;
-      const int64_t koff = (int64_t)dy * a.xs2 + (int64_t)dx * a.xs3 + cbase;
+      const int koff = dy * (int)a.xs2 + dx * (int)a.xs3 + cbase;
       const uint32_t sbase = stg + slot * TC_STG_SLOT;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int row = lrow + 8 * i;
         const bool ok = cok && (unsigned)(ih0[i] + dy) < (unsigned)a.h &&
                         (unsigned)(iw0[i] + dx) < (unsigned)a.w;
-        const float* src = ok ? a.x + (roff[i] + koff) : a.x;
+        const float* src = a.x + (ok ? roff[i] + koff : 0);
         const uint32_t dst = sbase + row * 64 + ((lchunk ^ ((row >> 1) & 3)) << 4);
         asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
                      "r"(ok ? 16 : 0)
@@ -713,11 +725,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               for (int e = 0; e < 4; ++e) rv[e] = c4 + e < a.kout ? __ldg(rrow + c4 + e) : 0.f;
             }
           }
+          float bv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (a.bias) {
+            if (full) {
+              const float4 t = *reinterpret_cast<const float4*>(bias_s + c4);
+              bv[0] = t.x; bv[1] = t.y; bv[2] = t.z; bv[3] = t.w;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) bv[e] = bias_s[min(c4 + e, a.kout - 1)];
+            }
+          }
           float o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             float val = tot[16 * j + 4 * v4 + e];
-            if (a.bias) val += bias_s[min(c4 + e, a.kout - 1)];
+            if (a.bias) val += bv[e];
             if (rrow && a.res_before_act) val += rv[e];
             val = tc_act(val, a.act);
             if (rrow && !a.res_before_act) val += rv[e];
@@ -875,6 +897,15 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   a.r = r; a.s = s; a.sh = p->stride_h; a.sw = p->stride_w; a.ph = p->pad_h; a.pw = p->pad_w;
   a.dh = p->dil_h; a.dw = p->dil_w;
   if (m_total > 0x7fffffffLL - TC_BM) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: too many output pixels");
+  {
+    // The A producers address the input with 32-bit element offsets: the
+    // furthest element any view coordinate (including padding taps, which are
+    // never read) can name must stay below 2^31.
+    const int64_t span = (n - 1) * x->stride[0] + (h + 2 * (int64_t)p->pad_h + (int64_t)p->dil_h * r) * x->stride[2] +
+                         (w + 2 * (int64_t)p->pad_w + (int64_t)p->dil_w * s) * x->stride[3] + c_pad;
+    if (span > 0x7fffffffLL || x->stride[2] > 0x7fffffffLL || x->stride[3] > 0x7fffffffLL)
+      return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: input too large for 32-bit offsets");
+  }
   if (k_out > TC_MAX_BIAS) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: too many output channels");
   a.m_total = (int)m_total;
   a.cb = c_pad / TC_BK;
