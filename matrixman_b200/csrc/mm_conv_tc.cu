@@ -40,6 +40,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -70,6 +71,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking test of a phase.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_addr(bar)), "r"(parity)
@@ -249,21 +263,31 @@ struct TcArgs {
   int oh, ow, kout;
   int r, s, sh, sw, ph, pw, dh, dw;
   int m_total;    // output pixels (fits in 31 bits; checked on the host)
-  int kb_total;  // r * s * (c_pad / 32)
-  int cb;        // c_pad / 32
-  int bn;        // N tile: multiple of 16, <= TC_MAX_BN
-  int n_tiles;   // ceil(kout / bn)
-  int64_t tiles; // m tiles * n tiles
-  int stages;    // pipeline depth (TMEM A stages == shared-memory B stages)
-  int period;    // k-blocks of hi*hi products accumulated in TMEM before promotion
+  int kb_total;   // r * s * (c_pad / 32)
+  int cb;         // c_pad / 32
+  int bn;         // N tile: multiple of 16, <= TC_MAX_BN
+  int n_tiles;    // ceil(kout / bn)
+  int amode;      // how A tiles arrive: TC_A_GATHER, TC_A_FLAT or TC_A_RECT
+  int tw, th;     // TC_A_RECT: output tile of th rows x tw columns (th * tw = 128)
+  int ntw, nth;   // TC_A_RECT: tiles across one output image
+  int64_t mtiles; // pixel tiles
+  int64_t tiles;  // mtiles * n_tiles
+  int stages;     // pipeline depth (A/B shared-memory stages == TMEM lo stages)
+  int xbuf;       // cross-term accumulator sets (2: the next tile's cross terms overlap the epilogue)
+  int period;     // k-blocks of hi*hi products accumulated in TMEM before promotion
   int act, res_before_act;
   int vec_store;  // output rows 16-byte aligned: float4 stores
   int res_vec;    // residual rows 16-byte aligned: float4 loads
 };
 
+// How the 128-pixel x 32-channel A tile of a k-block reaches shared memory.
+constexpr int TC_A_GATHER = 0;  // producer warps, 16-byte cp.async per pixel row (any geometry)
+constexpr int TC_A_FLAT = 1;    // one 2-D TMA load: 1x1, stride 1, no padding, uniform pixels
+constexpr int TC_A_RECT = 2;    // one 4-D TMA load of a th x tw pixel rectangle: stride 1
+
 // Warp roles of the persistent kernel.
 constexpr int TC_A_WARPS = 8;      // warps 0-7: A producers (2 per TMEM lane quarter)
-constexpr int TC_WARP_TMA = 8;     // warp 8: weight TMA
+constexpr int TC_WARP_TMA = 8;     // warp 8: TMA (weights; A in the TMA modes)
 constexpr int TC_WARP_HH = 9;      // warp 9: hi*hi MMA issue + TMEM owner
 constexpr int TC_WARP_HL = 10;     // warp 10: hi*lo MMA issue
 constexpr int TC_WARP_LH = 11;     // warp 11: lo*hi MMA issue
@@ -271,12 +295,11 @@ constexpr int TC_WARP_EPI = 12;    // warps 12-19: promotion + epilogue (2 per l
 constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_EPI_CHUNKS = 3;   // 16-column chunks per epilogue warp (bn <= 96)
 constexpr int TC_THREADS = (TC_WARP_EPI + TC_EPI_WARPS) * 32;
-constexpr int TC_STG_DEPTH = 4;    // k-blocks of A copies in flight per producer warp (power of 2)
-constexpr int TC_STG_SLOT = 32 * 64;  // one k-block of a producer warp: 32 rows x 64 B
 constexpr uint32_t TC_TMEM_COLS = 512;
-constexpr int TC_A_COLS = 64;      // TMEM columns per A stage (32 hi + 32 lo)
-constexpr int TC_MAX_BN = 80;      // N tile limit: 4 accumulators of bn columns + 3 A stages
-constexpr int TC_MAX_STAGES = 6;
+constexpr int TC_LO_COLS = 32;     // TMEM columns per lo stage
+constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 4;  // one A tile: 128 rows x 128 B
+constexpr int TC_MAX_BN = 80;      // N tile limit (4 accumulators of bn columns + lo stages)
+constexpr int TC_MAX_STAGES = 8;
 constexpr int TC_MAX_BIAS = 2048;  // output channels whose bias is staged in shared memory
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
@@ -320,51 +343,120 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
-// Shared-memory layout of one CTA (offsets from the 1024-aligned base).
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                            int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Shared-memory layout of one CTA (offsets from the 1024-aligned base).  A
+// stage holds the A tile (128 pixel rows x 128 B, 128-byte swizzle) and the B
+// hi and lo tiles (bn rows x 128 B each); every stage offset is a multiple of
+// 1024 bytes, as the swizzled layout requires.
 struct TcSmem {
-  uint32_t stage_bytes, staging, bias, bars;
+  uint32_t stage_bytes, bias, bars;
   int stages;
   __host__ __device__ static TcSmem make(int bn, int stages, int kout) {
     TcSmem l;
     l.stages = stages;
-    l.stage_bytes = 2u * (uint32_t)bn * 128u;           // B hi + lo tiles
-    l.staging = (uint32_t)stages * l.stage_bytes;        // A copy rings of the producer warps
-    l.bias = l.staging + TC_A_WARPS * TC_STG_DEPTH * TC_STG_SLOT;       // kout floats, 16-byte padded
+    l.stage_bytes = TC_A_BYTES + 2u * (uint32_t)bn * 128u;
+    l.bias = (uint32_t)stages * l.stage_bytes;           // kout floats, 16-byte padded
     l.bars = l.bias + (((uint32_t)kout * 4u + 15u) & ~15u);
     return l;
   }
-  // mbarriers: full_a[S], full_b[S], empty[S], hh_full[2], hh_free[2],
-  // cross_full, cross_free, drain[3]; then the TMEM address slot.
-  __host__ __device__ int n_bars() const { return 3 * stages + 9; }
+  // mbarriers: full_x[S], full_b[S], full_lo[S], empty[S], hh_full[2],
+  // hh_free[2], cross_full[2], cross_free[2], drain[3]; then the TMEM slot.
+  __host__ __device__ int n_bars() const { return 4 * stages + 11; }
   __host__ __device__ size_t bytes() const { return 1024 + bars + (size_t)n_bars() * 8 + 16; }
 };
 
-// One MMA issuer.  ROLE 0 (hi*hi) rotates between two period buffers that the
-// promotion warps fold into the fp32 total every `period` k-blocks; ROLE 1
-// (hi*lo) and ROLE 2 (lo*hi) accumulate a whole tile into one buffer each --
-// their partial sums are ~2^-11 of the result, so the tensor core's
-// round-toward-zero accumulation leaves no measurable drift there.
+// Origin of pixel tile `mt`: flat tiles start at pixel m0; rectangles at
+// (image n, output row oh0, output column ow0).
+struct TcTile {
+  int m0, n, oh0, ow0;
+};
+
+__device__ __forceinline__ TcTile tc_tile(const TcArgs& a, int mt) {
+  TcTile t;
+  if (a.amode == TC_A_RECT) {
+    const int per_img = a.nth * a.ntw;
+    t.n = mt / per_img;
+    const int rem = mt - t.n * per_img;
+    const int ty = rem / a.ntw;
+    t.oh0 = ty * a.th;
+    t.ow0 = (rem - ty * a.ntw) * a.tw;
+    t.m0 = 0;
+  } else {
+    t.m0 = mt * TC_BM;
+    t.n = t.oh0 = t.ow0 = 0;
+  }
+  return t;
+}
+
+// Output coordinates of tile row `row`; false when the row is outside the
+// output (last flat tile, or a rectangle overhanging the image edge).
+__device__ __forceinline__ bool tc_row(const TcArgs& a, const TcTile& t, int row, int& n, int& oh,
+                                       int& ow) {
+  if (a.amode == TC_A_RECT) {
+    const int ry = row / a.tw;
+    n = t.n;
+    oh = t.oh0 + ry;
+    ow = t.ow0 + (row - ry * a.tw);
+    return oh < a.oh && ow < a.ow;
+  }
+  const int m = t.m0 + row;
+  if (m >= a.m_total) return false;
+  const unsigned q = (unsigned)m / (unsigned)a.ow;
+  ow = (int)((unsigned)m - q * (unsigned)a.ow);
+  oh = (int)(q % (unsigned)a.oh);
+  n = (int)(q / (unsigned)a.oh);
+  return true;
+}
+
+// Byte offset of 16-byte chunk j of row `row` in a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t sw128_off(int row, int j) {
+  return (uint32_t)(row * 128 + ((j ^ (row & 7)) << 4));
+}
+
+// One MMA issuer.  ROLE 0 (hi*hi) and ROLE 1 (hi*lo) read the A tile straight
+// from shared memory: for fp32 data the tensor core uses the value truncated
+// to tf32, which is the high part of the split.  ROLE 2 (lo*hi) reads the
+// exact remainder x - trunc(x) that the producer warps wrote into a TMEM lo
+// stage.  ROLE 0 rotates between two period buffers that the promotion warps
+// fold into the fp32 total every `period` k-blocks; ROLE 1 and ROLE 2
+// accumulate a whole tile into one buffer each -- their partial sums are
+// ~2^-11 of the result, so the tensor core's round-toward-zero accumulation
+// leaves no measurable drift there.
 template <int ROLE>
 __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const TcSmem& L,
-                                         uint32_t tmem, uint64_t* full_a, uint64_t* full_b,
-                                         uint64_t* empty, uint64_t* hh_full, uint64_t* hh_free,
-                                         uint64_t* cross_full, uint64_t* cross_free,
-                                         uint64_t* drain) {
+                                         uint32_t tmem, uint64_t* full_x, uint64_t* full_b,
+                                         uint64_t* full_lo, uint64_t* empty, uint64_t* hh_full,
+                                         uint64_t* hh_free, uint64_t* cross_full,
+                                         uint64_t* cross_free, uint64_t* drain) {
   const int S = a.stages, KB = a.kb_total;
   const int NP = (KB + a.period - 1) / a.period;
   const uint32_t b_bytes = (uint32_t)a.bn * 128;
-  const uint32_t acc0 = (uint32_t)(TC_A_COLS * S);
+  const uint32_t acc0 = (uint32_t)(TC_LO_COLS * S);
   const uint32_t idesc = idesc_tf32(TC_BM, a.bn);
-  const uint32_t a_off = ROLE == 2 ? 32u : 0u;         // A lo plane for lo*hi
-  const uint32_t b_off = ROLE == 1 ? b_bytes : 0u;     // B lo plane for hi*lo
+  // B hi for hi*hi and lo*hi, B lo for hi*lo.
+  const uint32_t b_off = TC_A_BYTES + (ROLE == 1 ? b_bytes : 0u);
+  // cp.async writes the gathered tile through the generic proxy: the hi*hi and
+  // hi*lo MMAs then wait for full_lo, which every producer thread signals only
+  // after a proxy fence that makes its copies visible to the tensor core.
+  uint64_t* full_a = (ROLE == 2 || a.amode == TC_A_GATHER) ? full_lo : full_x;
   int64_t pc = 0, tc = 0;
   int st = 0;         // A/B stage of the next k-block
   uint32_t par = 0;   // its fill phase parity
   bool alive = true;
   for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x, ++tc) {
-    uint32_t d = tmem + acc0 + (uint32_t)((ROLE == 1 ? 2 : 3) * a.bn);
+    const int xb = a.xbuf == 2 ? (int)(tc & 1) : 0;
+    const uint32_t xpar = (uint32_t)((a.xbuf == 2 ? tc >> 1 : tc) & 1);
+    uint32_t d = tmem + acc0 + (uint32_t)((2 + 2 * xb + (ROLE == 1 ? 0 : 1)) * a.bn);
     if (ROLE != 0) {
-      if (!mbar_wait(cross_free, (uint32_t)(tc & 1) ^ 1u, TC_ERR_WAIT_ACC)) {
+      if (!mbar_wait(&cross_free[xb], xpar ^ 1u, TC_ERR_WAIT_ACC)) {
         alive = false;
         break;
       }
@@ -389,12 +481,18 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
           break;
         }
         tc_fence_after();
-        const uint32_t at = tmem + (uint32_t)(st * TC_A_COLS) + a_off;
-        const uint32_t bs = smem_addr(smem + (size_t)st * L.stage_bytes) + b_off;
+        const uint32_t stage = smem_addr(smem + (size_t)st * L.stage_bytes);
+        const uint32_t bs = stage + b_off;
         const bool first = ROLE == 0 ? kb == kb_begin : kb == 0;
 #pragma unroll
-        for (int k = 0; k < TC_BK / 8; ++k)
-          mma_tf32_ts(d, at + 8 * k, smem_desc_sw128(bs + 32 * k), idesc, (first && k == 0) ? 0u : 1u);
+        for (int k = 0; k < TC_BK / 8; ++k) {
+          const uint32_t acc = (first && k == 0) ? 0u : 1u;
+          if (ROLE == 2)
+            mma_tf32_ts(d, tmem + (uint32_t)(st * TC_LO_COLS + 8 * k), smem_desc_sw128(bs + 32 * k),
+                        idesc, acc);
+          else
+            mma_tf32(d, smem_desc_sw128(stage + 32 * k), smem_desc_sw128(bs + 32 * k), idesc, acc);
+        }
         mma_commit(&empty[st]);
         if (++st == S) {
           st = 0;
@@ -406,7 +504,7 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
         ++pc;
       }
     }
-    if (ROLE != 0 && alive) mma_commit(cross_full);
+    if (ROLE != 0 && alive) mma_commit(&cross_full[xb]);
   }
   if (!alive || tc_error_raised()) {
     // Error path: no MMA of this thread may still write TMEM when it is freed.
@@ -415,25 +513,108 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
   }
 }
 
+// Epilogue of one 16-column chunk of an output row: bias (shared memory),
+// residual (read-only path, RM 1 = added before the activation, 2 = after),
+// activation, store.  Activation and residual mode are template parameters,
+// so the 16 element chains carry no branches and interleave.
+template <int ACT>
+__device__ __forceinline__ float tc_act_t(float v) {
+  if (ACT == MM_ACT_RELU) return (v != v) ? v : (v > 0.f ? v : 0.f);
+  if (ACT == MM_ACT_SILU) return __fdividef(v, 1.0f + __expf(fminf(-v, 88.0f)));
+  if (ACT == MM_ACT_SIGMOID) return __fdividef(1.0f, 1.0f + __expf(fminf(-v, 88.0f)));
+  return v;
+}
+
+template <int ACT, int RM, int J>
+__device__ __forceinline__ void tc_finish_chunk(const TcArgs& a, float (&tot)[TC_EPI_CHUNKS * 16],
+                                                int h, int nchunk, int n0, const float* bias_s,
+                                                float* yrow, const float* rrow) {
+  const int c = h + 2 * J;
+  const int cb0 = n0 + 16 * c;
+  if (c >= nchunk || cb0 >= a.kout) return;
+  if (cb0 + 16 <= a.kout) {
+    float rv[16];
+    if (RM != 0) {
+      if (a.res_vec) {
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+          const float4 t = __ldg(reinterpret_cast<const float4*>(rrow + cb0) + v4);
+          rv[4 * v4] = t.x; rv[4 * v4 + 1] = t.y; rv[4 * v4 + 2] = t.z; rv[4 * v4 + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) rv[e] = __ldg(rrow + cb0 + e);
+      }
+    }
+#pragma unroll
+    for (int v4 = 0; v4 < 4; ++v4) {
+      const float4 b = *reinterpret_cast<const float4*>(bias_s + cb0 + 4 * v4);
+      const float bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * v4 + e;
+        float val = tot[16 * J + i] + bb[e];
+        if (RM == 1) val += rv[i];
+        val = tc_act_t<ACT>(val);
+        if (RM == 2) val += rv[i];
+        tot[16 * J + i] = val;
+      }
+    }
+    if (a.vec_store) {
+#pragma unroll
+      for (int v4 = 0; v4 < 4; ++v4)
+        reinterpret_cast<float4*>(yrow + cb0)[v4] =
+            make_float4(tot[16 * J + 4 * v4], tot[16 * J + 4 * v4 + 1], tot[16 * J + 4 * v4 + 2],
+                        tot[16 * J + 4 * v4 + 3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) yrow[cb0 + e] = tot[16 * J + e];
+    }
+    return;
+  }
+  // Last, partial chunk of an output width that is not a multiple of 16.
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int cc = cb0 + e;
+    if (cc < a.kout) {
+      float val = tot[16 * J + e] + bias_s[cc];
+      if (RM == 1) val += __ldg(rrow + cc);
+      val = tc_act_t<ACT>(val);
+      if (RM == 2) val += __ldg(rrow + cc);
+      yrow[cc] = val;
+    }
+  }
+}
+
+template <int ACT, int RM>
+__device__ __forceinline__ void tc_finish_row(const TcArgs& a, float (&tot)[TC_EPI_CHUNKS * 16],
+                                              int h, int nchunk, int n0, const float* bias_s,
+                                              float* yrow, const float* rrow) {
+  tc_finish_chunk<ACT, RM, 0>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);
+  tc_finish_chunk<ACT, RM, 1>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);
+  tc_finish_chunk<ACT, RM, 2>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);
+}
+
 __global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap_hi,
-                   const __grid_constant__ CUtensorMap wmap_lo, const TcArgs a) {
+                   const __grid_constant__ CUtensorMap wmap_lo,
+                   const __grid_constant__ CUtensorMap amap, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int S = a.stages;
   const TcSmem L = TcSmem::make(a.bn, S, a.kout);
   float* bias_s = (float*)(smem + L.bias);
   const uint32_t b_bytes = (uint32_t)a.bn * 128;
-  uint8_t* staging = smem + L.staging;
   uint64_t* bars = (uint64_t*)(smem + L.bars);
-  uint64_t* full_a = bars;                // S: 256 producer arrivals (A stage written to TMEM)
-  uint64_t* full_b = bars + S;            // S: TMA transaction bytes
-  uint64_t* empty = bars + 2 * S;         // S: one commit per issuer frees the A/B stage
-  uint64_t* hh_full = bars + 3 * S;       // 2: hi*hi period complete in TMEM
-  uint64_t* hh_free = bars + 3 * S + 2;   // 2: one arrival per promotion thread
-  uint64_t* cross_full = bars + 3 * S + 4;  // hi*lo and lo*hi tile sums complete
-  uint64_t* cross_free = bars + 3 * S + 5;  // one arrival per epilogue thread
-  uint64_t* drain = bars + 3 * S + 6;       // 3: issuer error paths wait for their MMAs
+  uint64_t* full_x = bars;                // S: A tile in shared memory
+  uint64_t* full_b = bars + S;            // S: B tiles (TMA transaction bytes)
+  uint64_t* full_lo = bars + 2 * S;       // S: lo plane in TMEM (one arrival per producer thread)
+  uint64_t* empty = bars + 3 * S;         // S: one commit per issuer frees the stage
+  uint64_t* hh_full = bars + 4 * S;       // 2: hi*hi period complete in TMEM
+  uint64_t* hh_free = bars + 4 * S + 2;   // 2: one arrival per promotion thread
+  uint64_t* cross_full = bars + 4 * S + 4;  // 2: hi*lo and lo*hi tile sums complete
+  uint64_t* cross_free = bars + 4 * S + 6;  // 2: one arrival per epilogue thread
+  uint64_t* drain = bars + 4 * S + 8;       // 3: issuer error paths wait for their MMAs
   uint32_t* tmem_slot = (uint32_t*)(bars + L.n_bars());
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -444,16 +625,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full_a[i], TC_A_WARPS * 32);
+      // Gather mode: every producer thread's cp.async completion arrives
+      // (.noinc); TMA modes: the TMA thread's arrive + transaction bytes.
+      mbar_init(&full_x[i], a.amode == TC_A_GATHER ? TC_A_WARPS * 32 : 1);
       mbar_init(&full_b[i], 1);
+      mbar_init(&full_lo[i], TC_A_WARPS * 32);
       mbar_init(&empty[i], 3);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&hh_full[i], 1);
       mbar_init(&hh_free[i], 32 * TC_EPI_WARPS);
     }
-    mbar_init(cross_full, 2);
-    mbar_init(cross_free, 32 * TC_EPI_WARPS);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&cross_full[i], 2);
+      mbar_init(&cross_free[i], 32 * TC_EPI_WARPS);
+    }
     for (int i = 0; i < 3; ++i) mbar_init(&drain[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -464,172 +650,227 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (a.bias)
-    for (int i = threadIdx.x; i < a.kout; i += TC_THREADS) bias_s[i] = a.bias[i];
+  for (int i = threadIdx.x; i < a.kout; i += TC_THREADS) bias_s[i] = a.bias ? a.bias[i] : 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: A stages at [64 s, 64 s + 64) (hi then lo); from acc0 = 64 S
-  // the hi*hi period buffers [acc0, acc0 + 2 bn), the hi*lo tile sum
-  // [acc0 + 2 bn, acc0 + 3 bn) and the lo*hi tile sum [acc0 + 3 bn, acc0 + 4 bn).
-  const uint32_t acc0 = (uint32_t)(TC_A_COLS * S);
+  // TMEM columns: lo stages at [32 s, 32 s + 32); from acc0 = 32 S the hi*hi
+  // period buffers [acc0, acc0 + 2 bn), then xbuf cross-term sets of 2 bn
+  // columns (hi*lo tile sum, then lo*hi tile sum).
+  const uint32_t acc0 = (uint32_t)(TC_LO_COLS * S);
   const int KB = a.kb_total;
   const int NP = (KB + a.period - 1) / a.period;
+  const int64_t my_tiles = a.tiles > blockIdx.x ? (a.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t total = my_tiles * KB;
 
   if (warp < TC_A_WARPS) {
-    // ---------------- A producers: cp.async gather -> split -> TMEM ----------------
+    // ---------------- A producers ----------------
     // Warp w owns TMEM lane quarter q = w % 4 (tile rows 32 q .. 32 q + 31) and
-    // channel half h = w / 4 of every 32-channel k-block.  Each k-block's 32
-    // rows x 64 B arrive by 16-byte cp.async (zero-filled for padding taps,
-    // rows past the end and padded channels) in a private ring of
-    // TC_STG_DEPTH slots that runs ahead across tile boundaries; a slot is
-    // XOR swizzled so both the copies (8 rows x 64 B) and the per-row reads
-    // are conflict-free.  Each lane then splits its row into tf32 high part
-    // and exact remainder and writes both planes to the TMEM A stage.
+    // channel half h = w / 4 (16 channels) of every 32-channel k-block.
     const int q = warp & 3;
     const int half = warp >> 2;
-    const int lrow = lane >> 2;
-    const int lchunk = lane & 3;
-    const uint32_t stg = smem_addr(staging + warp * (TC_STG_DEPTH * TC_STG_SLOT));
     const uint32_t tm_rows = tmem + ((uint32_t)(q * 32) << 16);
-    const int64_t my_tiles = a.tiles > blockIdx.x ? (a.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const int64_t total = my_tiles * KB;
-    // Prefetch cursor: tile, k-block position (tap r, tap s, channel block) and
-    // the per-row input coordinates of that tile.  Row offsets include this
-    // lane's channel offset; a k-block adds one offset uniform over the warp.
-    int64_t ptile = blockIdx.x;
-    int pkr = 0, pks = 0, pcb = 0;
-    const int lane_c = half * 16 + lchunk * 4;
-    int roff[4];  // element offsets (the input spans < 2^31 elements; checked on the host)
-    int ih0[4], iw0[4];
-    auto setup_rows = [&]() {
-      const int m0 = (int)(ptile / a.n_tiles) * TC_BM + q * 32;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int m = m0 + lrow + 8 * i;
-        const bool ok = m < a.m_total;
-        const unsigned mm_ = ok ? (unsigned)m : 0u;
-        const int ow_ = (int)(mm_ % (unsigned)a.ow);
-        const unsigned qq = mm_ / (unsigned)a.ow;
-        const int oh_ = (int)(qq % (unsigned)a.oh);
-        // Rows past the end get a coordinate that fails the bounds test.
-        ih0[i] = ok ? oh_ * a.sh - a.ph : -0x40000000;
-        iw0[i] = ow_ * a.sw - a.pw;
-        // Rows past the end keep an in-range base: their copies are zero-filled.
-        roff[i] = ok ? (int)((qq / (unsigned)a.oh) * (unsigned)a.xs0) + ih0[i] * (int)a.xs2 +
-                           iw0[i] * (int)a.xs3 + lane_c
-                     : 0;
-      }
-    };
-    // Issue the copies of the cursor's k-block into `slot` and advance it.
-    auto prefetch = [&](int slot) {
-      const int dy = pkr * a.dh, dx = pks * a.dw;
-      const int cbase = pcb * TC_BK;
-      const bool cok = cbase + lane_c < a.c;
-      const int koff = dy * (int)a.xs2 + dx * (int)a.xs3 + cbase;
-      const uint32_t sbase = stg + slot * TC_STG_SLOT;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = lrow + 8 * i;
-        const bool ok = cok && (unsigned)(ih0[i] + dy) < (unsigned)a.h &&
-                        (unsigned)(iw0[i] + dx) < (unsigned)a.w;
-        const float* src = a.x + (ok ? roff[i] + koff : 0);
-        const uint32_t dst = sbase + row * 64 + ((lchunk ^ ((row >> 1) & 3)) << 4);
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-                     "r"(ok ? 16 : 0)
-                     : "memory");
-      }
-      if (++pcb == a.cb) {
-        pcb = 0;
-        if (++pks == a.s) {
-          pks = 0;
-          if (++pkr == a.r) {
-            pkr = 0;
-            ptile += gridDim.x;
-            if (ptile < a.tiles) setup_rows();
-          }
-        }
-      }
-    };
-    if (total > 0) setup_rows();
-#pragma unroll
-    for (int d = 0; d < TC_STG_DEPTH; ++d) {
-      if (d < total) prefetch(d);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    }
+    const uint32_t stage0 = smem_addr(smem);
     int st = 0;
     uint32_t par = 0;
-    for (int64_t g = 0; g < total; ++g) {
-      const int slot = (int)(g & (TC_STG_DEPTH - 1));
-      asm volatile("cp.async.wait_group %0;" ::"n"(TC_STG_DEPTH - 1) : "memory");
-      __syncwarp();
-      float hi[16], lo[16];
+    if (a.amode == TC_A_GATHER) {
+      // Gather: 16-byte cp.async of this warp's 32 rows x 64 B into the
+      // swizzled A tile, zero-filled for padding taps, rows outside the output
+      // and padded channels, run `ahead` k-blocks in front of the split.
+      const int lrow = lane >> 2;
+      const int lchunk = lane & 3;
+      const int lane_c = half * 16 + lchunk * 4;
+      const int ahead = S - 1;  // k-blocks loaded beyond the one being split
+      int64_t ltile = blockIdx.x;
+      int lkr = 0, lks = 0, lcb = 0;
+      int lst = 0;
+      uint32_t lpar = 0;
+      int roff[4];  // element offsets (the input spans < 2^31 elements; checked on the host)
+      int ih0[4], iw0[4];
+      auto setup_rows = [&]() {
+        const TcTile t = tc_tile(a, (int)(ltile / a.n_tiles));
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        float4 v;
-        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                     : "r"(stg + slot * TC_STG_SLOT + lane * 64 + ((c4 ^ ((lane >> 1) & 3)) << 4)));
-        const float4 hv = split_hi(v);
-        hi[4 * c4 + 0] = hv.x; hi[4 * c4 + 1] = hv.y; hi[4 * c4 + 2] = hv.z; hi[4 * c4 + 3] = hv.w;
-        lo[4 * c4 + 0] = v.x - hv.x; lo[4 * c4 + 1] = v.y - hv.y;
-        lo[4 * c4 + 2] = v.z - hv.z; lo[4 * c4 + 3] = v.w - hv.w;
+        for (int i = 0; i < 4; ++i) {
+          int n_ = 0, oh_ = 0, ow_ = 0;
+          const bool ok = tc_row(a, t, q * 32 + lrow + 8 * i, n_, oh_, ow_);
+          // Rows outside the output get a coordinate that fails the bounds test.
+          ih0[i] = ok ? oh_ * a.sh - a.ph : -0x40000000;
+          iw0[i] = ow_ * a.sw - a.pw;
+          roff[i] = ok ? n_ * (int)a.xs0 + ih0[i] * (int)a.xs2 + iw0[i] * (int)a.xs3 + lane_c : 0;
+        }
+      };
+      bool alive = true;
+      // Issue the copies of the load cursor's k-block and advance the cursor.
+      auto load_next = [&]() -> bool {
+        if (!mbar_wait(&empty[lst], lpar ^ 1u, TC_ERR_WAIT_EMPTY)) return false;
+
+        const int dy = lkr * a.dh, dx = lks * a.dw;
+        const int cbase = lcb * TC_BK;
+        const bool cok = cbase + lane_c < a.c;
+        const int koff = dy * (int)a.xs2 + dx * (int)a.xs3 + cbase;
+        const uint32_t tile_s = stage0 + (uint32_t)lst * L.stage_bytes;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = q * 32 + lrow + 8 * i;
+          const bool ok = cok && (unsigned)(ih0[i] + dy) < (unsigned)a.h &&
+                          (unsigned)(iw0[i] + dx) < (unsigned)a.w;
+          const float* src = a.x + (ok ? roff[i] + koff : 0);
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(
+                           tile_s + sw128_off(row, half * 4 + lchunk)),
+                       "l"(src), "r"(ok ? 16 : 0)
+                       : "memory");
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(
+                         smem_addr(&full_x[lst]))
+                     : "memory");
+        if (++lst == S) {
+          lst = 0;
+          lpar ^= 1u;
+        }
+        if (++lcb == a.cb) {
+          lcb = 0;
+          if (++lks == a.s) {
+            lks = 0;
+            if (++lkr == a.r) {
+              lkr = 0;
+              ltile += gridDim.x;
+              if (ltile < a.tiles) setup_rows();
+            }
+          }
+        }
+        return true;
+      };
+      if (total > 0) setup_rows();
+      int64_t issued = 0;
+      for (int64_t g = 0; g < total && alive; ++g) {
+        // k-block g must be in flight; later k-blocks are issued while their
+        // stage is already free (lane 0 tests, the warp follows; every lane
+        // then takes the barrier itself, which succeeds at once).
+        while (alive && issued <= g) {
+          alive = load_next();
+          ++issued;
+        }
+        while (alive && issued < total && issued < g + ahead &&
+               __shfl_sync(0xffffffffu, mbar_test(&empty[lst], lpar ^ 1u) ? 1 : 0, 0)) {
+          alive = load_next();
+          ++issued;
+        }
+        if (!alive) break;
+        if (!mbar_wait(&full_x[st], par, TC_ERR_WAIT_A)) break;
+        fence_proxy_async_smem();
+        float lo[16];
+        const uint32_t tile_s = stage0 + (uint32_t)st * L.stage_bytes;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float4 v;
+          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                       : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                       : "r"(tile_s + sw128_off(q * 32 + lane, half * 4 + c4)));
+          lo[4 * c4 + 0] = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+          lo[4 * c4 + 1] = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+          lo[4 * c4 + 2] = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+          lo[4 * c4 + 3] = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+        }
+        tmem_st16(tm_rows + (uint32_t)(st * TC_LO_COLS + half * 16), lo);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        mbar_arrive(&full_lo[st]);
+        if (++st == S) {
+          st = 0;
+          par ^= 1u;
+        }
       }
-      __syncwarp();
-      if (g + TC_STG_DEPTH < total) prefetch(slot);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      if (!mbar_wait(&empty[st], par ^ 1u, TC_ERR_WAIT_EMPTY)) break;
-      const uint32_t col = (uint32_t)(st * TC_A_COLS + half * 16);
-      tmem_st16(tm_rows + col, hi);
-      tmem_st16(tm_rows + col + 32, lo);
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      tc_fence_before();
-      mbar_arrive(&full_a[st]);
-      if (++st == S) {
-        st = 0;
-        par ^= 1u;
+      // No copy may land in shared memory after the CTA has exited.
+      asm volatile("cp.async.wait_all;" ::: "memory");
+    } else {
+      // TMA modes: the A tile arrives by TMA; only the remainder is computed.
+      for (int64_t g = 0; g < total; ++g) {
+        if (!mbar_wait(&full_x[st], par, TC_ERR_WAIT_A)) break;
+        float lo[16];
+        const uint32_t tile_s = stage0 + (uint32_t)st * L.stage_bytes;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float4 v;
+          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                       : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                       : "r"(tile_s + sw128_off(q * 32 + lane, half * 4 + c4)));
+          lo[4 * c4 + 0] = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+          lo[4 * c4 + 1] = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+          lo[4 * c4 + 2] = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+          lo[4 * c4 + 3] = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+        }
+        tmem_st16(tm_rows + (uint32_t)(st * TC_LO_COLS + half * 16), lo);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        mbar_arrive(&full_lo[st]);
+        if (++st == S) {
+          st = 0;
+          par ^= 1u;
+        }
       }
     }
-    // No copy may land in shared memory after the CTA has exited.
-    asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == TC_WARP_TMA) {
-    // ---------------- weights via TMA ----------------
+    // ---------------- TMA: weights, and the A tile in the TMA modes ----------------
     if (lane == 0) {
       int64_t g = 0;
       int st = 0;
       uint32_t par = 0;
       bool alive = true;
       for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x) {
+        const TcTile t = tc_tile(a, (int)(tile / a.n_tiles));
         const int n0 = (int)(tile % a.n_tiles) * a.bn;
+        int kr = 0, ks = 0, cbk = 0;
         for (int kb = 0; kb < KB; ++kb, ++g) {
           if (!mbar_wait(&empty[st], par ^ 1u, TC_ERR_WAIT_EMPTY)) {
             alive = false;
             break;
           }
-          uint8_t* bhi = smem + (size_t)st * L.stage_bytes;
+          uint8_t* stage = smem + (size_t)st * L.stage_bytes;
+          if (a.amode == TC_A_FLAT) {
+            mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES);
+            tma_load_2d(stage, &amap, &full_x[st], cbk * TC_BK, t.m0);
+          } else if (a.amode == TC_A_RECT) {
+            // Taps outside the image read as zero (TMA out-of-bounds fill).
+            mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES);
+            tma_load_4d(stage, &amap, &full_x[st], cbk * TC_BK, t.ow0 - a.pw + ks * a.dw,
+                        t.oh0 - a.ph + kr * a.dh, t.n);
+          }
           mbar_arrive_expect_tx(&full_b[st], 2 * b_bytes);
-          tma_load_2d(bhi, &wmap_hi, &full_b[st], kb * TC_BK, n0);
-          tma_load_2d(bhi + b_bytes, &wmap_lo, &full_b[st], kb * TC_BK, n0);
+          tma_load_2d(stage + TC_A_BYTES, &wmap_hi, &full_b[st], kb * TC_BK, n0);
+          tma_load_2d(stage + TC_A_BYTES + b_bytes, &wmap_lo, &full_b[st], kb * TC_BK, n0);
           if (++st == S) {
             st = 0;
             par ^= 1u;
           }
+          if (++cbk == a.cb) {
+            cbk = 0;
+            if (++ks == a.s) {
+              ks = 0;
+              ++kr;
+            }
+          }
         }
       }
       // Bulk copies must not outlive the CTA's shared memory.
-      for (int64_t k = (g > S ? g - S : 0); k < g; ++k)
-        mbar_wait(&full_b[k % S], (uint32_t)((k / S) & 1), TC_ERR_WAIT_B);
+      for (int64_t k = (g > S ? g - S : 0); k < g; ++k) {
+        const uint32_t kp = (uint32_t)((k / S) & 1);
+        mbar_wait(&full_b[k % S], kp, TC_ERR_WAIT_B);
+        if (a.amode != TC_A_GATHER) mbar_wait(&full_x[k % S], kp, TC_ERR_WAIT_A);
+      }
     }
   } else if (warp == TC_WARP_HH) {
     if (lane == 0)
-      tc_issue<0>(a, smem, L, tmem, full_a, full_b, empty, hh_full, hh_free, cross_full, cross_free, drain);
+      tc_issue<0>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
+                  cross_free, drain);
   } else if (warp == TC_WARP_HL) {
     if (lane == 0)
-      tc_issue<1>(a, smem, L, tmem, full_a, full_b, empty, hh_full, hh_free, cross_full, cross_free, drain);
+      tc_issue<1>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
+                  cross_free, drain);
   } else if (warp == TC_WARP_LH) {
     if (lane == 0)
-      tc_issue<2>(a, smem, L, tmem, full_a, full_b, empty, hh_full, hh_free, cross_full, cross_free, drain);
+      tc_issue<2>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
+                  cross_free, drain);
   } else if (warp >= TC_WARP_EPI) {
     // ---------------- promotion (fp32 RN adds) + epilogue ----------------
     // Two warps per TMEM lane quarter; warp half h owns the 16-column chunks
@@ -668,12 +909,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         mbar_arrive(&hh_free[b]);
       }
       if (!alive) break;
-      if (!mbar_wait(cross_full, (uint32_t)(tc & 1), TC_ERR_WAIT_ACC)) {
+      const int xb = a.xbuf == 2 ? (int)(tc & 1) : 0;
+      if (!mbar_wait(&cross_full[xb], (uint32_t)((a.xbuf == 2 ? tc >> 1 : tc) & 1), TC_ERR_WAIT_ACC)) {
         alive = false;
         break;
       }
       tc_fence_after();
-      const uint32_t cross = lane_base + acc0 + (uint32_t)(2 * a.bn);
+      const uint32_t cross = lane_base + acc0 + (uint32_t)((2 + 2 * xb) * a.bn);
 #pragma unroll
       for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
         const int c = h + 2 * j;
@@ -689,71 +931,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(cross_free);
+      mbar_arrive(&cross_free[xb]);
       if (g_tc_error != 0) continue;
 
-      const int m0 = (int)(tile / a.n_tiles) * TC_BM;
+      const TcTile t = tc_tile(a, (int)(tile / a.n_tiles));
       const int n0 = (int)(tile % a.n_tiles) * a.bn;
-      const int m = m0 + q * 32 + lane;
-      if (m >= a.m_total) continue;
-      const unsigned ow_ = (unsigned)m % (unsigned)a.ow;
-      const unsigned qq = (unsigned)m / (unsigned)a.ow;
-      const unsigned oh_ = qq % (unsigned)a.oh;
-      const unsigned n_ = qq / (unsigned)a.oh;
+      int n_ = 0, oh_ = 0, ow_ = 0;
+      if (!tc_row(a, t, q * 32 + lane, n_, oh_, ow_)) continue;
       float* yrow = a.y + ((int64_t)n_ * a.ys0 + (int64_t)oh_ * a.ys2 + (int64_t)ow_ * a.ys3);
       const float* rrow =
           a.res ? a.res + ((int64_t)n_ * a.rs0 + (int64_t)oh_ * a.rs2 + (int64_t)ow_ * a.rs3) : nullptr;
-      // Bias comes from shared memory and the residual through the read-only
-      // path, so no global load has to wait behind a store that might alias it.
-#pragma unroll
-      for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
-        const int c = h + 2 * j;
-        const int cb0 = n0 + 16 * c;
-        if (c >= nchunk || cb0 >= a.kout) break;
-#pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4) {
-          const int c4 = cb0 + 4 * v4;
-          if (c4 >= a.kout) break;
-          const bool full = c4 + 4 <= a.kout;
-          float rv[4] = {0.f, 0.f, 0.f, 0.f};
-          if (rrow) {
-            if (a.res_vec && full) {
-              const float4 t = __ldg(reinterpret_cast<const float4*>(rrow + c4));
-              rv[0] = t.x; rv[1] = t.y; rv[2] = t.z; rv[3] = t.w;
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) rv[e] = c4 + e < a.kout ? __ldg(rrow + c4 + e) : 0.f;
-            }
-          }
-          float bv[4] = {0.f, 0.f, 0.f, 0.f};
-          if (a.bias) {
-            if (full) {
-              const float4 t = *reinterpret_cast<const float4*>(bias_s + c4);
-              bv[0] = t.x; bv[1] = t.y; bv[2] = t.z; bv[3] = t.w;
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) bv[e] = bias_s[min(c4 + e, a.kout - 1)];
-            }
-          }
-          float o[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float val = tot[16 * j + 4 * v4 + e];
-            if (a.bias) val += bv[e];
-            if (rrow && a.res_before_act) val += rv[e];
-            val = tc_act(val, a.act);
-            if (rrow && !a.res_before_act) val += rv[e];
-            o[e] = val;
-          }
-          if (a.vec_store && full) {
-            *reinterpret_cast<float4*>(yrow + c4) = make_float4(o[0], o[1], o[2], o[3]);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (c4 + e < a.kout) yrow[c4 + e] = o[e];
-          }
-        }
+      const int rm = rrow ? (a.res_before_act ? 1 : 2) : 0;
+#define MM_TC_FINISH(ACT)                                                             \
+  if (rm == 0) tc_finish_row<ACT, 0>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);      \
+  else if (rm == 1) tc_finish_row<ACT, 1>(a, tot, h, nchunk, n0, bias_s, yrow, rrow); \
+  else tc_finish_row<ACT, 2>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);
+      switch (a.act) {
+        case MM_ACT_RELU: MM_TC_FINISH(MM_ACT_RELU) break;
+        case MM_ACT_SILU: MM_TC_FINISH(MM_ACT_SILU) break;
+        case MM_ACT_SIGMOID: MM_TC_FINISH(MM_ACT_SIGMOID) break;
+        default: MM_TC_FINISH(MM_ACT_NONE) break;
       }
+#undef MM_TC_FINISH
     }
   }
 
@@ -792,6 +991,33 @@ struct MapKeyHash {
 std::mutex g_map_mu;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
+// cuTensorMapEncodeTiled, resolved through the runtime so the library does
+// not link libcuda (it must load on hosts without a driver).
+int encode_tiled(const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                 const cuuint32_t* box, CUtensorMap* out) {
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn encode = nullptr;
+  if (encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess)
+      return fail(MM_ERR_CUDA, "mm_conv2d_tc: cuTensorMapEncodeTiled entry point unavailable");
+    encode = (EncodeFn)fn;
+  }
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, (void*)base, dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MM_ERR_CUDA, "mm_conv2d_tc: cuTensorMapEncodeTiled failed (CUresult " +
+                                 std::to_string((int)r) + ")");
+  return MM_OK;
+}
+
 // 2-D tensor map over a [kpad rows][ktot cols] fp32 weight plane, box
 // {32 cols (128 bytes), bn rows}, 128B swizzle.  Rows beyond kpad read as 0.
 int weight_map(const float* w, int64_t ktot, int64_t kpad, int bn, CUtensorMap* out) {
@@ -806,32 +1032,12 @@ int weight_map(const float* w, int64_t ktot, int64_t kpad, int bn, CUtensorMap* 
       return MM_OK;
     }
   }
-  // The driver entry point is resolved through the runtime so the library does
-  // not link libcuda (it must load on hosts without a driver).
-  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-  static EncodeFn encode = nullptr;
-  if (encode == nullptr) {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess)
-      return fail(MM_ERR_CUDA, "mm_conv2d_tc: cuTensorMapEncodeTiled entry point unavailable");
-    encode = (EncodeFn)fn;
-  }
   CUtensorMap map;
-  cuuint64_t dims[2] = {(cuuint64_t)ktot, (cuuint64_t)kpad};
-  cuuint64_t strides[1] = {(cuuint64_t)ktot * 4};
-  cuuint32_t box[2] = {32, (cuuint32_t)bn};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)w, dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(MM_ERR_CUDA, "mm_conv2d_tc: cuTensorMapEncodeTiled failed (CUresult " +
-                                 std::to_string((int)r) + ")");
+  const cuuint64_t dims[2] = {(cuuint64_t)ktot, (cuuint64_t)kpad};
+  const cuuint64_t strides[1] = {(cuuint64_t)ktot * 4};
+  const cuuint32_t box[2] = {32, (cuuint32_t)bn};
+  int rc = encode_tiled(w, 2, dims, strides, box, &map);
+  if (rc != MM_OK) return rc;
   std::lock_guard<std::mutex> g(g_map_mu);
   g_maps[key] = map;
   *out = map;
@@ -839,6 +1045,24 @@ int weight_map(const float* w, int64_t ktot, int64_t kpad, int bn, CUtensorMap* 
 }
 
 bool aligned16(const void* p) { return (((uintptr_t)p) & 15) == 0; }
+
+// Dynamic shared memory one CTA may request on the current device: the
+// opt-in maximum minus the kernel's static shared memory.
+int tc_smem_limit(int dev, size_t* out) {
+  static size_t cached[256] = {};
+  if (dev < 0 || dev >= 256) return fail(MM_ERR_INVALID, "mm_conv2d_tc: device index");
+  if (cached[dev] == 0) {
+    int optin = 0;
+    MM_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev),
+            "mm_conv2d_tc: shared memory limit");
+    cudaFuncAttributes fa;
+    MM_CUDA(cudaFuncGetAttributes(&fa, conv_tc_kernel), "mm_conv2d_tc: kernel attributes");
+    if ((size_t)optin <= fa.sharedSizeBytes) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: shared memory");
+    cached[dev] = (size_t)optin - fa.sharedSizeBytes;
+  }
+  *out = cached[dev];
+  return MM_OK;
+}
 
 bool nhwc_ok(const mm_tensor_t* t) {
   return t->ndim == 4 && t->stride[1] == 1 && t->stride[0] % 4 == 0 && t->stride[2] % 4 == 0 &&
@@ -922,11 +1146,74 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   a.res_before_act = p->residual_before_act;
   a.vec_store = nhwc_ok(y) ? 1 : 0;
   a.res_vec = residual && nhwc_ok(residual) ? 1 : 0;
-  // TMEM (512 columns): S A stages of 64 columns plus four accumulators of bn
-  // columns (two hi*hi period buffers, the hi*lo and lo*hi tile sums).
-  int stages = (int)((TC_TMEM_COLS - 4 * a.bn) / TC_A_COLS);
-  if (stages > TC_MAX_STAGES) stages = TC_MAX_STAGES;
-  if (stages < 2) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: N tile too wide for TMEM");
+  // How A tiles arrive (see TC_A_*).  Rectangles are chosen when they cover
+  // the output with little overhang.
+  a.amode = TC_A_GATHER;
+  a.tw = a.th = a.ntw = a.nth = 1;
+  {
+    const bool stride1 = p->stride_h == 1 && p->stride_w == 1;
+    const bool uniform = x->stride[2] == w * x->stride[3] && x->stride[0] == h * x->stride[2];
+    if (stride1 && r == 1 && s == 1 && p->pad_h == 0 && p->pad_w == 0 && uniform &&
+        n * h * w <= 0x7fffffffLL) {
+      a.amode = TC_A_FLAT;
+    } else if (stride1) {
+      double best = 0.0;
+      for (int tw = 128; tw >= 4; tw /= 2) {
+        const int th = TC_BM / tw;
+        const int64_t ntw = (ow + tw - 1) / tw, nth = (oh + th - 1) / th;
+        const double eff = (double)(oh * ow) / (double)(ntw * tw * nth * th);
+        if (eff > best + 1e-9) {
+          best = eff;
+          a.tw = tw;
+          a.th = th;
+          a.ntw = (int)ntw;
+          a.nth = (int)nth;
+        }
+      }
+      if (best >= 0.8 && (int64_t)n * a.ntw * a.nth <= 0x7fffffffLL) a.amode = TC_A_RECT;
+    }
+  }
+  // A tensor map for the TMA modes (a map the driver rejects falls back to
+  // the gather mode).
+  CUtensorMap amap;
+  memset(&amap, 0, sizeof(amap));
+  if (a.amode == TC_A_FLAT) {
+    // [pixels][C] rows; channels past C and pixels past the end read as zero.
+    const cuuint64_t dims[2] = {(cuuint64_t)c_in, (cuuint64_t)(n * h * w)};
+    const cuuint64_t strides[1] = {(cuuint64_t)x->stride[3] * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BM};
+    if (encode_tiled(x->data, 2, dims, strides, box, &amap) != MM_OK) a.amode = TC_A_GATHER;
+  } else if (a.amode == TC_A_RECT) {
+    // {C, W, H, N}; coordinates outside the image (padding taps) read as zero.
+    const cuuint64_t dims[4] = {(cuuint64_t)c_in, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
+    const cuuint64_t strides[3] = {(cuuint64_t)x->stride[3] * 4, (cuuint64_t)x->stride[2] * 4,
+                                   (cuuint64_t)x->stride[0] * 4};
+    const cuuint32_t box[4] = {(cuuint32_t)TC_BK, (cuuint32_t)a.tw, (cuuint32_t)a.th, 1};
+    if (encode_tiled(x->data, 4, dims, strides, box, &amap) != MM_OK) a.amode = TC_A_GATHER;
+  }
+
+  a.mtiles = a.amode == TC_A_RECT ? n * (int64_t)a.ntw * a.nth : (m_total + TC_BM - 1) / TC_BM;
+  a.tiles = a.mtiles * a.n_tiles;
+  // Stages: TMEM holds S lo stages of 32 columns plus four accumulators of bn
+  // columns (two hi*hi period buffers, the hi*lo and lo*hi tile sums); shared
+  // memory holds S (A + B hi + B lo) stages, the bias and the barriers.
+  int dev = 0;
+  MM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  size_t smem_limit = 0;
+  if ((rc = tc_smem_limit(dev, &smem_limit)) != MM_OK) return rc;
+  // Two cross-term sets when at least 4 stages still fit, else one.
+  int stages = 0;
+  for (int xbuf = 2; xbuf >= 1 && stages == 0; --xbuf) {
+    for (int st = TC_MAX_STAGES; st >= (xbuf == 2 ? 4 : 3); --st) {
+      if (TC_LO_COLS * st + (2 + 2 * xbuf) * a.bn <= (int)TC_TMEM_COLS &&
+          TcSmem::make(a.bn, st, k_out).bytes() <= smem_limit) {
+        stages = st;
+        a.xbuf = xbuf;
+        break;
+      }
+    }
+  }
+  if (stages == 0) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: N tile too wide");
   a.stages = stages;
   const int64_t ktot = (int64_t)r * s * c_pad;
   size_t smem = TcSmem::make(a.bn, stages, k_out).bytes();
@@ -934,25 +1221,21 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   CUtensorMap mhi, mlo;
   if ((rc = weight_map(w_hi, ktot, k_pad, a.bn, &mhi)) != MM_OK) return rc;
   if ((rc = weight_map(w_lo, ktot, k_pad, a.bn, &mlo)) != MM_OK) return rc;
-
   // The kernel owns all 512 TMEM columns, so a second resident CTA on an SM
   // would stall in tcgen05.alloc until the first exits: pad the shared-memory
   // request whenever the occupancy calculator allows more than one CTA.
-  int dev = 0;
-  MM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   {
     static size_t configured[256] = {};
     static size_t min_smem[256] = {};
     std::lock_guard<std::mutex> g(g_map_mu);
     if (dev < 0 || dev >= 256) return fail(MM_ERR_INVALID, "mm_conv2d_tc: device index");
     if (configured[dev] == 0) {
-      const size_t full = 200 * 1024;
+      const size_t full = smem_limit;
       MM_CUDA(cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)full),
               "mm_conv2d_tc: shared memory attribute");
       configured[dev] = full;
-      size_t lo = 16 * 1024;
-      for (size_t req = lo; req <= full; req += 4096) {
+      for (size_t req = 16 * 1024; req <= full; req += 4096) {
         int blocks = 0;
         MM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, conv_tc_kernel, TC_THREADS, req),
                 "mm_conv2d_tc: occupancy");
@@ -966,11 +1249,9 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
     if (smem < min_smem[dev]) smem = min_smem[dev];
     if (smem > configured[dev]) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: shared memory");
   }
-  const int64_t mt = (m_total + TC_BM - 1) / TC_BM;
-  a.tiles = mt * a.n_tiles;
   // Persistent CTAs: one per SM.
   const int64_t ctas = a.tiles < (int64_t)sm_count() ? a.tiles : (int64_t)sm_count();
-  conv_tc_kernel<<<(unsigned)ctas, TC_THREADS, smem, resolve_stream(stream)>>>(mhi, mlo, a);
+  conv_tc_kernel<<<(unsigned)ctas, TC_THREADS, smem, resolve_stream(stream)>>>(mhi, mlo, amap, a);
   MM_LAUNCH_CHECK("mm_conv2d_tc launch");
   return MM_OK;
 }
