@@ -283,7 +283,8 @@ struct TcArgs {
 // How the 128-pixel x 32-channel A tile of a k-block reaches shared memory.
 constexpr int TC_A_GATHER = 0;  // producer warps, 16-byte cp.async per pixel row (any geometry)
 constexpr int TC_A_FLAT = 1;    // one 2-D TMA load: 1x1, stride 1, no padding, uniform pixels
-constexpr int TC_A_RECT = 2;    // one 4-D TMA load of a th x tw pixel rectangle: stride 1
+constexpr int TC_A_RECT = 2;    // one 4-D TMA load of a th x tw output-pixel rectangle
+                                // (conv strides become TMA traversal strides)
 
 // Warp roles of the persistent kernel.
 constexpr int TC_A_WARPS = 8;      // warps 0-7: A producers (2 per TMEM lane quarter)
@@ -833,8 +834,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           } else if (a.amode == TC_A_RECT) {
             // Taps outside the image read as zero (TMA out-of-bounds fill).
             mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES);
-            tma_load_4d(stage, &amap, &full_x[st], cbk * TC_BK, t.ow0 - a.pw + ks * a.dw,
-                        t.oh0 - a.ph + kr * a.dh, t.n);
+            tma_load_4d(stage, &amap, &full_x[st], cbk * TC_BK, t.ow0 * a.sw - a.pw + ks * a.dw,
+                        t.oh0 * a.sh - a.ph + kr * a.dh, t.n);
           }
           mbar_arrive_expect_tx(&full_b[st], 2 * b_bytes);
           tma_load_2d(stage + TC_A_BYTES, &wmap_hi, &full_b[st], kb * TC_BK, n0);
@@ -993,8 +994,10 @@ std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
 // cuTensorMapEncodeTiled, resolved through the runtime so the library does
 // not link libcuda (it must load on hosts without a driver).
+// `estr` (traversal strides, default 1): a box dimension of b elements with
+// traversal stride t brings ceil(b / t) elements, stored densely.
 int encode_tiled(const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
-                 const cuuint32_t* box, CUtensorMap* out) {
+                 const cuuint32_t* box, CUtensorMap* out, const cuuint32_t* estr = nullptr) {
   using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -1008,9 +1011,9 @@ int encode_tiled(const void* base, int rank, const cuuint64_t* dims, const cuuin
       return fail(MM_ERR_CUDA, "mm_conv2d_tc: cuTensorMapEncodeTiled entry point unavailable");
     encode = (EncodeFn)fn;
   }
-  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const cuuint32_t ones[5] = {1, 1, 1, 1, 1};
   CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, (void*)base, dims,
-                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      strides, box, estr ? estr : ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(MM_ERR_CUDA, "mm_conv2d_tc: cuTensorMapEncodeTiled failed (CUresult " +
@@ -1152,14 +1155,17 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   a.tw = a.th = a.ntw = a.nth = 1;
   {
     const bool stride1 = p->stride_h == 1 && p->stride_w == 1;
+    // TMA traversal strides go up to 8; the box spans tw * stride input columns.
+    const bool strided_ok = p->stride_h <= 8 && p->stride_w <= 8;
     const bool uniform = x->stride[2] == w * x->stride[3] && x->stride[0] == h * x->stride[2];
     if (stride1 && r == 1 && s == 1 && p->pad_h == 0 && p->pad_w == 0 && uniform &&
         n * h * w <= 0x7fffffffLL) {
       a.amode = TC_A_FLAT;
-    } else if (stride1) {
+    } else if (strided_ok) {
       double best = 0.0;
       for (int tw = 128; tw >= 4; tw /= 2) {
         const int th = TC_BM / tw;
+        if (tw * p->stride_w > 256 || th * p->stride_h > 256) continue;
         const int64_t ntw = (ow + tw - 1) / tw, nth = (oh + th - 1) / th;
         const double eff = (double)(oh * ow) / (double)(ntw * tw * nth * th);
         if (eff > best + 1e-9) {
@@ -1188,8 +1194,10 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
     const cuuint64_t dims[4] = {(cuuint64_t)c_in, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
     const cuuint64_t strides[3] = {(cuuint64_t)x->stride[3] * 4, (cuuint64_t)x->stride[2] * 4,
                                    (cuuint64_t)x->stride[0] * 4};
-    const cuuint32_t box[4] = {(cuuint32_t)TC_BK, (cuuint32_t)a.tw, (cuuint32_t)a.th, 1};
-    if (encode_tiled(x->data, 4, dims, strides, box, &amap) != MM_OK) a.amode = TC_A_GATHER;
+    const cuuint32_t box[4] = {(cuuint32_t)TC_BK, (cuuint32_t)(a.tw * p->stride_w),
+                               (cuuint32_t)(a.th * p->stride_h), 1};
+    const cuuint32_t estr[4] = {1, (cuuint32_t)p->stride_w, (cuuint32_t)p->stride_h, 1};
+    if (encode_tiled(x->data, 4, dims, strides, box, &amap, estr) != MM_OK) a.amode = TC_A_GATHER;
   }
 
   a.mtiles = a.amode == TC_A_RECT ? n * (int64_t)a.ntw * a.nth : (m_total + TC_BM - 1) / TC_BM;
