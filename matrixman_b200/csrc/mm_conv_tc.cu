@@ -251,6 +251,26 @@ __device__ __forceinline__ float4 split_hi(float4 v) {
   return make_float4(tf32_rna_int(v.x), tf32_rna_int(v.y), tf32_rna_int(v.z), tf32_rna_int(v.w));
 }
 
+// Division of n < 2^31 by a runtime divisor d as a multiply and shift:
+// with s = ceil(log2 d) and m = ceil(2^(31+s) / d), floor(n * m / 2^(31+s))
+// equals floor(n / d) (the rounding error of m stays below 1/d).
+struct FastDiv {
+  uint32_t d, m, s;
+};
+
+__host__ __device__ inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f;
+  f.d = d;
+  f.s = 0;
+  while ((1u << f.s) < d) ++f.s;
+  f.m = (uint32_t)(((1ull << (31 + f.s)) + d - 1) / d);
+  return f;
+}
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+  return (uint32_t)(((uint64_t)n * f.m) >> (31 + f.s));
+}
+
 struct TcArgs {
   const float* x;
   int64_t xs0, xs2, xs3;  // NHWC pixel strides (channel stride is 1)
@@ -278,6 +298,7 @@ struct TcArgs {
   int act, res_before_act;
   int vec_store;  // output rows 16-byte aligned: float4 stores
   int res_vec;    // residual rows 16-byte aligned: float4 loads
+  FastDiv div_ow, div_oh, div_img, div_ntw;  // output width, height; rectangles per image, per row
 };
 
 // How the 128-pixel x 32-channel A tile of a k-block reaches shared memory.
@@ -384,9 +405,9 @@ __device__ __forceinline__ TcTile tc_tile(const TcArgs& a, int mt) {
   TcTile t;
   if (a.amode == TC_A_RECT) {
     const int per_img = a.nth * a.ntw;
-    t.n = mt / per_img;
+    t.n = (int)fdiv((uint32_t)mt, a.div_img);
     const int rem = mt - t.n * per_img;
-    const int ty = rem / a.ntw;
+    const int ty = (int)fdiv((uint32_t)rem, a.div_ntw);
     t.oh0 = ty * a.th;
     t.ow0 = (rem - ty * a.ntw) * a.tw;
     t.m0 = 0;
@@ -410,10 +431,10 @@ __device__ __forceinline__ bool tc_row(const TcArgs& a, const TcTile& t, int row
   }
   const int m = t.m0 + row;
   if (m >= a.m_total) return false;
-  const unsigned q = (unsigned)m / (unsigned)a.ow;
-  ow = (int)((unsigned)m - q * (unsigned)a.ow);
-  oh = (int)(q % (unsigned)a.oh);
-  n = (int)(q / (unsigned)a.oh);
+  const uint32_t q = fdiv((uint32_t)m, a.div_ow);
+  ow = (int)((uint32_t)m - q * (uint32_t)a.ow);
+  n = (int)fdiv(q, a.div_oh);
+  oh = (int)(q - (uint32_t)n * (uint32_t)a.oh);
   return true;
 }
 
@@ -886,6 +907,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     bool alive = true;
     for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x, ++tc) {
       float tot[TC_EPI_CHUNKS * 16];
+      const int xb = a.xbuf == 2 ? (int)(tc & 1) : 0;
+      const uint32_t xpar = (uint32_t)((a.xbuf == 2 ? tc >> 1 : tc) & 1);
+      const uint32_t cross = lane_base + acc0 + (uint32_t)((2 + 2 * xb) * a.bn);
       for (int p = 0; p < NP; ++p, ++pc) {
         const int b = (int)(pc & 1);
         if (!mbar_wait(&hh_full[b], (uint32_t)((pc >> 1) & 1), TC_ERR_WAIT_ACC)) {
@@ -910,13 +934,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         mbar_arrive(&hh_free[b]);
       }
       if (!alive) break;
-      const int xb = a.xbuf == 2 ? (int)(tc & 1) : 0;
-      if (!mbar_wait(&cross_full[xb], (uint32_t)((a.xbuf == 2 ? tc >> 1 : tc) & 1), TC_ERR_WAIT_ACC)) {
+      if (!mbar_wait(&cross_full[xb], xpar, TC_ERR_WAIT_ACC)) {
         alive = false;
         break;
       }
       tc_fence_after();
-      const uint32_t cross = lane_base + acc0 + (uint32_t)((2 + 2 * xb) * a.bn);
 #pragma unroll
       for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
         const int c = h + 2 * j;
@@ -933,7 +955,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       tc_fence_before();
       mbar_arrive(&cross_free[xb]);
-      if (g_tc_error != 0) continue;
 
       const TcTile t = tc_tile(a, (int)(tile / a.n_tiles));
       const int n0 = (int)(tile % a.n_tiles) * a.bn;
@@ -1200,6 +1221,10 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
     if (encode_tiled(x->data, 4, dims, strides, box, &amap, estr) != MM_OK) a.amode = TC_A_GATHER;
   }
 
+  a.div_ow = make_fastdiv((uint32_t)a.ow);
+  a.div_oh = make_fastdiv((uint32_t)a.oh);
+  a.div_img = make_fastdiv((uint32_t)(a.ntw * a.nth));
+  a.div_ntw = make_fastdiv((uint32_t)a.ntw);
   a.mtiles = a.amode == TC_A_RECT ? n * (int64_t)a.ntw * a.nth : (m_total + TC_BM - 1) / TC_BM;
   a.tiles = a.mtiles * a.n_tiles;
   // Stages: TMEM holds S lo stages of 32 columns plus four accumulators of bn
