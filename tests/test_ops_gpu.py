@@ -291,3 +291,27 @@ def test_batch_norm_eval(mm, golden):
         assert max_rel_err(bn(nhwc(mm, x)).cpu(), bn(x)) < 1e-6
     with pytest.raises(NotImplementedError):
         F.batch_norm(dev(mm, x), bn.running_mean, bn.running_var, training=True)
+
+
+@pytest.mark.parametrize("nc,hw,batch,layout", [
+    (80, (8, 4, 2), 3, "nhwc"),   # 84 anchors per image: 32-anchor chunks straddle levels and images
+    (5, (6, 3), 2, "nchw"),       # generic strides, small class count
+])
+def test_yolo_decode_matches_oracle(mm, nc, hw, batch, layout):
+    import ctypes
+    from matrixman_b200 import _lib, ops
+    g = gen(nc + batch)
+    reg_max = 16
+    no = 4 * reg_max + nc
+    strides = [8.0 * 2 ** i for i in range(len(hw))]
+    feats = [torch.randn(batch, no, s, s, generator=g) * 3 for s in hw]
+    ref = O.yolo_decode(feats, strides, reg_max, nc)
+    devs = [nhwc(mm, f) if layout == "nhwc" else dev(mm, f) for f in feats]
+    anchors = sum(s * s for s in hw)
+    out = ops.empty(devs[0].runtime, (batch, 4 + nc, anchors))
+    descs = [d.desc() for d in devs]
+    arr = (ctypes.POINTER(_lib.MMTensor) * len(descs))(*[ctypes.pointer(d) for d in descs])
+    st = (ctypes.c_float * len(strides))(*strides)
+    ops._launch("mm_yolo_decode", arr, st, len(devs), reg_max, nc, ctypes.byref(out.desc()),
+                devs[0].runtime.stream)
+    assert max_rel_err(out.cpu(), ref) < CONV_GEMM_REL
