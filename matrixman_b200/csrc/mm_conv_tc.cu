@@ -294,6 +294,8 @@ struct TcArgs {
   int64_t tiles;  // mtiles * n_tiles
   int stages;     // pipeline depth (A/B shared-memory stages == TMEM lo stages)
   int xbuf;       // cross-term accumulator sets (2: the next tile's cross terms overlap the epilogue)
+  int epi_groups; // 2: two groups of 4 epilogue warps take alternate tiles (needs one hi*hi
+                  // period per tile, xbuf == 2 and bn <= 48, so each group owns its buffers)
   int period;     // k-blocks of hi*hi products accumulated in TMEM before promotion
   int act, res_before_act;
   int vec_store;  // output rows 16-byte aligned: float4 stores
@@ -551,7 +553,7 @@ template <int ACT, int RM, int J>
 __device__ __forceinline__ void tc_finish_chunk(const TcArgs& a, float (&tot)[TC_EPI_CHUNKS * 16],
                                                 int h, int nchunk, int n0, const float* bias_s,
                                                 float* yrow, const float* rrow) {
-  const int c = h + 2 * J;
+  const int c = a.epi_groups == 2 ? J : h + 2 * J;
   const int cb0 = n0 + 16 * c;
   if (c >= nchunk || cb0 >= a.kout) return;
   if (cb0 + 16 <= a.kout) {
@@ -656,11 +658,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&hh_full[i], 1);
-      mbar_init(&hh_free[i], 32 * TC_EPI_WARPS);
+      mbar_init(&hh_free[i], 32 * (a.epi_groups == 2 ? TC_EPI_WARPS / 2 : TC_EPI_WARPS));
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&cross_full[i], 2);
-      mbar_init(&cross_free[i], 32 * TC_EPI_WARPS);
+      mbar_init(&cross_free[i], 32 * (a.epi_groups == 2 ? TC_EPI_WARPS / 2 : TC_EPI_WARPS));
     }
     for (int i = 0; i < 3; ++i) mbar_init(&drain[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -899,19 +901,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // h, h + 2, h + 4 of the tile.  The fp32 total of a tile lives in
     // registers (one output row per thread), indexed with compile-time
     // offsets only.
+    // Split mode: warp half h owns chunks h, h + 2, h + 4 of every tile.
+    // Group mode: group g (warps g*4 .. g*4+3) owns all chunks of every other
+    // tile, so two tiles' epilogues overlap.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int h = (warp - TC_WARP_EPI) >> 2;
+    const bool grp = a.epi_groups == 2;
+    const int eg = (warp - TC_WARP_EPI) >> 2;
+    const int h = grp ? 0 : eg;
+    const int cstep = grp ? 1 : 2;
+    const int tstep = grp ? 2 : 1;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const int nchunk = a.bn >> 4;
-    int64_t pc = 0, tc = 0;
+    int64_t tc = grp ? eg : 0;
     bool alive = true;
-    for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x, ++tc) {
+    for (int64_t tile = blockIdx.x + tc * gridDim.x; tile < a.tiles && alive;
+         tile += tstep * (int64_t)gridDim.x, tc += tstep) {
       float tot[TC_EPI_CHUNKS * 16];
+      int64_t pc = tc * NP;  // this tile's first hi*hi period
       const int xb = a.xbuf == 2 ? (int)(tc & 1) : 0;
       const uint32_t xpar = (uint32_t)((a.xbuf == 2 ? tc >> 1 : tc) & 1);
       const uint32_t cross = lane_base + acc0 + (uint32_t)((2 + 2 * xb) * a.bn);
       for (int p = 0; p < NP; ++p, ++pc) {
-        const int b = (int)(pc & 1);
+        const int b = (int)(pc & 1);  // (in group mode NP == 1: buffer = tile parity = group)
         if (!mbar_wait(&hh_full[b], (uint32_t)((pc >> 1) & 1), TC_ERR_WAIT_ACC)) {
           alive = false;
           break;
@@ -920,7 +931,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t buf = lane_base + acc0 + (uint32_t)(b * a.bn);
 #pragma unroll
         for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
-          const int c = h + 2 * j;
+          const int c = h + cstep * j;
           if (c < nchunk) {
             uint32_t v[16];
             tmem_ld16_nowait(buf + (uint32_t)(16 * c), v);
@@ -941,7 +952,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_after();
 #pragma unroll
       for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
-        const int c = h + 2 * j;
+        const int c = h + cstep * j;
         if (c < nchunk) {
           uint32_t u[16], w[16];
           tmem_ld16_nowait(cross + (uint32_t)(16 * c), u);
@@ -1165,7 +1176,9 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
     a.bn = ((per + 15) / 16) * 16;
   }
   a.n_tiles = (k_out + a.bn - 1) / a.bn;
-  a.period = 4;
+  // Promotion period: 4 k-blocks; reductions of up to 12 k-blocks (48 hi*hi
+  // MMAs per accumulator, drift < 2e-6 relative) take one period per tile.
+  a.period = a.kb_total <= 12 ? a.kb_total : 4;
   a.act = p->act;
   a.res_before_act = p->residual_before_act;
   a.vec_store = nhwc_ok(y) ? 1 : 0;
@@ -1248,6 +1261,7 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   }
   if (stages == 0) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: N tile too wide");
   a.stages = stages;
+  a.epi_groups = (a.period >= a.kb_total && a.xbuf == 2 && a.bn <= 16 * TC_EPI_CHUNKS) ? 2 : 1;
   const int64_t ktot = (int64_t)r * s * c_pad;
   size_t smem = TcSmem::make(a.bn, stages, k_out).bytes();
 
