@@ -46,6 +46,8 @@ def parse_args():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--batch", type=int, default=BATCH)
     p.add_argument("--e2e-steps", type=int, default=None)
+    p.add_argument("--e2e-chunks", type=int, default=3,
+                   help="1 GPU: matrixman.infer chunks (upload / forward / readback overlap)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile-case", action="store_true",
                    help="run --steps eager forwards (no graphs, no timing) for an ncu capture")
@@ -262,6 +264,9 @@ def run_b200(args):
     x_pinned.copy_(x_host)
 
     def e2e_step():
+        if world == 1:
+            # The public batch API: CPU batch in, CPU result out.
+            return matrixman.infer(prepared, x_pinned, chunks=args.e2e_chunks, device=local)
         y = step(matrixman.to_device(x_pinned, device=local))
         return y.cpu() if y is not None else None
 
@@ -281,7 +286,9 @@ def run_b200(args):
     out_numel = batch * (4 + NC) * ANCHORS * world
     e2e = {"value": world * batch / e2e_s, "unit": UNIT,
            "h2d_bytes_per_step": int(x_host.numel() * 4) * world,
-           "d2h_bytes_per_step": int(out_numel * 4), "ms_per_step": e2e_s * 1e3}
+           "d2h_bytes_per_step": int(out_numel * 4), "ms_per_step": e2e_s * 1e3,
+           "api": (f"matrixman.infer(prepared, pinned batch, chunks={args.e2e_chunks})" if world == 1
+                   else "prepared(to_device(pinned slice)) + gather on rank 0 + .cpu()")}
     return {"world": world, "rank": rank, "local": local, "value": value, "ms_step": ms_step,
             "clocks": clock_info, "e2e": e2e, "launch_calls": launch_calls, "prepared": prepared,
             "x_dev": x_dev, "model": model, "macs": macs_per_image(model), "batch": batch,

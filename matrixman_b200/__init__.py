@@ -32,6 +32,7 @@ from .api import (
     to_gm45,
     unsupported_report,
 )
+from .pipeline import infer
 from .preparation import auto_prepare, prepare, prepare_cuda, prepare_opengl
 from .tensor import Gm45Tensor, MatrixManTensor, install_tensor_method, is_matrixman_tensor
 
@@ -96,6 +97,7 @@ class _MatrixManModule(types.ModuleType):
 sys.modules[__name__].__class__ = _MatrixManModule
 
 __all__ = [
+    "infer",
     "MatrixManTensor", "Gm45Tensor", "auto_prepare", "config", "debug_enabled", "device_count",
     "gpu_postprocess_detection", "init", "install_tensor_method", "is_gm45_tensor",
     "is_matrixman_tensor", "prefer", "prepare", "prepare_cuda", "prepare_opengl", "profile",

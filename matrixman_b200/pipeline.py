@@ -1,0 +1,133 @@
+"""Batch inference with uploads, compute and readbacks overlapped.
+
+The reference's flow is strictly serial: upload (``to_device``), forward,
+explicit ``.cpu()`` readback (``backends/cuda/backend.py:146-157``,
+``tensor.py:76-158``).  ``infer`` keeps that contract -- CPU batch in, CPU
+result out, values identical to ``model(to_device(x)).cpu()`` -- but splits the
+batch into chunks that travel on three streams of the device: host-to-device
+copies on an upload stream, the prepared forward on the runtime stream, and
+device-to-host copies on a readback stream, ordered by events.  While chunk k
+computes, chunk k+1 uploads and chunk k-1 reads back (the two copy directions
+use separate copy engines).  From page-locked host memory
+(``matrixman.pinned_empty``) every copy is asynchronous.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib, runtime
+from .replicas import batch_slices
+from .tensor import MatrixManTensor, contiguous_strides
+
+_aux_streams: dict[int, tuple[int, int]] = {}
+
+
+def _streams(rt) -> tuple[int, int]:
+    s = _aux_streams.get(rt.index)
+    if s is None:
+        lib = _lib.load()
+        up, down = ctypes.c_void_p(), ctypes.c_void_p()
+        runtime.set_device(rt.index)
+        _lib.check(lib.mm_stream_create(rt.index, ctypes.byref(up)), "stream create")
+        _lib.check(lib.mm_stream_create(rt.index, ctypes.byref(down)), "stream create")
+        s = (up.value, down.value)
+        _aux_streams[rt.index] = s
+    return s
+
+
+class _Events:
+    def __init__(self, n: int):
+        lib = _lib.load()
+        self.handles = []
+        for _ in range(n):
+            h = ctypes.c_void_p()
+            _lib.check(lib.mm_event_create(ctypes.byref(h), 0), "event create")
+            self.handles.append(h)
+
+    def __getitem__(self, i):
+        return self.handles[i]
+
+    def close(self):
+        lib = _lib.load()
+        for h in self.handles:
+            lib.mm_event_destroy(h)
+        self.handles = []
+
+
+def infer(model, x: torch.Tensor, chunks: int = 3, device=None) -> torch.Tensor:
+    """``model(to_device(x)).cpu()`` for a CPU batch ``x``, with the batch split
+    into ``chunks`` slices whose uploads, forwards and readbacks overlap.
+
+    ``model`` should be a prepared module (``matrixman.prepare``); its output
+    must be one tensor with the batch as its first dimension.  The result is
+    a CPU tensor (in pooled page-locked memory when available)."""
+    from .api import _device_index, get_backend
+
+    get_backend()
+    if not isinstance(x, torch.Tensor) or x.device.type != "cpu":
+        raise TypeError("MatrixMan: infer expects a CPU batch tensor")
+    if x.dtype != torch.float32:
+        raise TypeError("MatrixMan: infer supports float32 input only")
+    if x.dim() < 1 or x.shape[0] == 0:
+        raise ValueError("MatrixMan: infer needs a non-empty batch")
+    x = x.contiguous()
+    rt = runtime.get_runtime(_device_index(device))
+    runtime.set_device(rt.index)
+    lib = _lib.load()
+    up, down = _streams(rt)
+    slices = [sl for sl in batch_slices(int(x.shape[0]), max(1, int(chunks))) if sl[1] > sl[0]]
+    ev = _Events(3 * len(slices))
+    row = x[0].numel()
+    keep = []
+    out = None
+    try:
+        with torch.no_grad():
+            # All input blocks first: they are ordered on the runtime stream, so
+            # one event after the allocations lets the upload stream write
+            # them without waiting for any forward enqueued later.
+            inputs = []
+            for s, e in slices:
+                shape = (e - s,) + tuple(int(v) for v in x.shape[1:])
+                inputs.append((shape, rt.new_storage((e - s) * row, torch.float32)))
+            _lib.check(lib.mm_event_record(ev[0], rt.stream), "event record")
+            _lib.check(lib.mm_stream_wait_event(up, ev[0]), "stream wait")
+            for k, ((s, e), (shape, storage)) in enumerate(zip(slices, inputs)):
+                src = x.data_ptr() + s * row * 4
+                _lib.check(lib.mm_memcpy_h2d(ctypes.c_void_p(storage.pointer), ctypes.c_void_p(src),
+                                             (e - s) * row * 4, up, 0), "host-to-device copy")
+                _lib.check(lib.mm_event_record(ev[3 * k + 1], up), "event record")
+            for k, ((s, e), (shape, storage)) in enumerate(zip(slices, inputs)):
+                _lib.check(lib.mm_stream_wait_event(rt.stream, ev[3 * k + 1]), "stream wait")
+                xd = MatrixManTensor._from_owner(storage, shape, 0, contiguous_strides(shape))
+                y = model(xd)
+                if not isinstance(y, MatrixManTensor):
+                    raise NotImplementedError("MatrixMan: infer needs a model with one tensor output")
+                if tuple(y._logical_strides) != contiguous_strides(tuple(int(v) for v in y.shape)):
+                    from . import ops
+                    y = ops.materialize(y)
+                if out is None:
+                    out = runtime.host_empty((int(x.shape[0]),) + tuple(int(v) for v in y.shape[1:]),
+                                             torch.float32)
+                yrow = 1
+                for v in y.shape[1:]:
+                    yrow *= int(v)
+                _lib.check(lib.mm_event_record(ev[3 * k + 2], rt.stream), "event record")
+                _lib.check(lib.mm_stream_wait_event(down, ev[3 * k + 2]), "stream wait")
+                _lib.check(lib.mm_memcpy_d2h(ctypes.c_void_p(out.data_ptr() + s * yrow * 4),
+                                             ctypes.c_void_p(y.element_ptr), (e - s) * yrow * 4,
+                                             down, 0), "device-to-host copy")
+                # Device blocks are released only after the readback stream is
+                # done with them (below).
+                keep.append((xd, y))
+        _lib.check(lib.mm_stream_sync(ctypes.c_void_p(down), runtime.config.waitTimeoutMs), "synchronize")
+    finally:
+        try:
+            lib.mm_stream_sync(ctypes.c_void_p(down), runtime.config.waitTimeoutMs)
+            lib.mm_stream_sync(ctypes.c_void_p(up), runtime.config.waitTimeoutMs)
+        finally:
+            ev.close()
+    del keep
+    return out
