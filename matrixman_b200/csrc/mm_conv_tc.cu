@@ -619,6 +619,10 @@ __device__ __forceinline__ void tc_finish_row(const TcArgs& a, float (&tot)[TC_E
   tc_finish_chunk<ACT, RM, 2>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);
 }
 
+// One instantiation per activation and residual mode (RM 0 none, 1 added
+// before the activation, 2 after): each carries a single epilogue, which keeps
+// the code that the producer, TMA and MMA warps run beside it small.
+template <int ACT, int RM>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap_hi,
                    const __grid_constant__ CUtensorMap wmap_lo,
@@ -973,19 +977,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!tc_row(a, t, q * 32 + lane, n_, oh_, ow_)) continue;
       float* yrow = a.y + ((int64_t)n_ * a.ys0 + (int64_t)oh_ * a.ys2 + (int64_t)ow_ * a.ys3);
       const float* rrow =
-          a.res ? a.res + ((int64_t)n_ * a.rs0 + (int64_t)oh_ * a.rs2 + (int64_t)ow_ * a.rs3) : nullptr;
-      const int rm = rrow ? (a.res_before_act ? 1 : 2) : 0;
-#define MM_TC_FINISH(ACT)                                                             \
-  if (rm == 0) tc_finish_row<ACT, 0>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);      \
-  else if (rm == 1) tc_finish_row<ACT, 1>(a, tot, h, nchunk, n0, bias_s, yrow, rrow); \
-  else tc_finish_row<ACT, 2>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);
-      switch (a.act) {
-        case MM_ACT_RELU: MM_TC_FINISH(MM_ACT_RELU) break;
-        case MM_ACT_SILU: MM_TC_FINISH(MM_ACT_SILU) break;
-        case MM_ACT_SIGMOID: MM_TC_FINISH(MM_ACT_SIGMOID) break;
-        default: MM_TC_FINISH(MM_ACT_NONE) break;
-      }
-#undef MM_TC_FINISH
+          RM != 0 ? a.res + ((int64_t)n_ * a.rs0 + (int64_t)oh_ * a.rs2 + (int64_t)ow_ * a.rs3)
+                  : nullptr;
+      tc_finish_row<ACT, RM>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);
     }
   }
 
@@ -1083,6 +1077,26 @@ bool aligned16(const void* p) { return (((uintptr_t)p) & 15) == 0; }
 
 // Dynamic shared memory one CTA may request on the current device: the
 // opt-in maximum minus the kernel's static shared memory.
+using TcKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const TcArgs);
+constexpr int TC_VARIANTS = 12;  // 4 activations x 3 residual modes
+
+template <int ACT>
+TcKernel tc_kernel_rm(int rm) {
+  return rm == 1 ? conv_tc_kernel<ACT, 1> : rm == 2 ? conv_tc_kernel<ACT, 2> : conv_tc_kernel<ACT, 0>;
+}
+
+// Variant v = 3 * act + rm; activation codes other than the four named ones
+// apply no activation.
+TcKernel tc_kernel(int v) {
+  const int act = v / 3, rm = v % 3;
+  switch (act) {
+    case MM_ACT_RELU: return tc_kernel_rm<MM_ACT_RELU>(rm);
+    case MM_ACT_SILU: return tc_kernel_rm<MM_ACT_SILU>(rm);
+    case MM_ACT_SIGMOID: return tc_kernel_rm<MM_ACT_SIGMOID>(rm);
+    default: return tc_kernel_rm<MM_ACT_NONE>(rm);
+  }
+}
+
 int tc_smem_limit(int dev, size_t* out) {
   static size_t cached[256] = {};
   if (dev < 0 || dev >= 256) return fail(MM_ERR_INVALID, "mm_conv2d_tc: device index");
@@ -1090,10 +1104,14 @@ int tc_smem_limit(int dev, size_t* out) {
     int optin = 0;
     MM_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev),
             "mm_conv2d_tc: shared memory limit");
-    cudaFuncAttributes fa;
-    MM_CUDA(cudaFuncGetAttributes(&fa, conv_tc_kernel), "mm_conv2d_tc: kernel attributes");
-    if ((size_t)optin <= fa.sharedSizeBytes) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: shared memory");
-    cached[dev] = (size_t)optin - fa.sharedSizeBytes;
+    size_t static_smem = 0;
+    for (int v = 0; v < TC_VARIANTS; ++v) {
+      cudaFuncAttributes fa;
+      MM_CUDA(cudaFuncGetAttributes(&fa, tc_kernel(v)), "mm_conv2d_tc: kernel attributes");
+      if (fa.sharedSizeBytes > static_smem) static_smem = fa.sharedSizeBytes;
+    }
+    if ((size_t)optin <= static_smem) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: shared memory");
+    cached[dev] = (size_t)optin - static_smem;
   }
   *out = cached[dev];
   return MM_OK;
@@ -1271,34 +1289,36 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   // The kernel owns all 512 TMEM columns, so a second resident CTA on an SM
   // would stall in tcgen05.alloc until the first exits: pad the shared-memory
   // request whenever the occupancy calculator allows more than one CTA.
+  const int variant = 3 * (a.act >= 0 && a.act <= MM_ACT_SIGMOID ? a.act : MM_ACT_NONE) +
+                      (a.res ? (a.res_before_act ? 1 : 2) : 0);
+  const TcKernel kernel = tc_kernel(variant);
   {
-    static size_t configured[256] = {};
-    static size_t min_smem[256] = {};
+    static size_t configured[256][TC_VARIANTS] = {};
+    static size_t min_smem[256][TC_VARIANTS] = {};
     std::lock_guard<std::mutex> g(g_map_mu);
     if (dev < 0 || dev >= 256) return fail(MM_ERR_INVALID, "mm_conv2d_tc: device index");
-    if (configured[dev] == 0) {
+    if (configured[dev][variant] == 0) {
       const size_t full = smem_limit;
-      MM_CUDA(cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)full),
+      MM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)full),
               "mm_conv2d_tc: shared memory attribute");
-      configured[dev] = full;
+      configured[dev][variant] = full;
       for (size_t req = 16 * 1024; req <= full; req += 4096) {
         int blocks = 0;
-        MM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, conv_tc_kernel, TC_THREADS, req),
+        MM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, TC_THREADS, req),
                 "mm_conv2d_tc: occupancy");
         if (blocks <= 1) {
-          min_smem[dev] = req;
+          min_smem[dev][variant] = req;
           break;
         }
       }
-      if (min_smem[dev] == 0) min_smem[dev] = full;
+      if (min_smem[dev][variant] == 0) min_smem[dev][variant] = full;
     }
-    if (smem < min_smem[dev]) smem = min_smem[dev];
-    if (smem > configured[dev]) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: shared memory");
+    if (smem < min_smem[dev][variant]) smem = min_smem[dev][variant];
+    if (smem > configured[dev][variant]) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: shared memory");
   }
   // Persistent CTAs: one per SM.
   const int64_t ctas = a.tiles < (int64_t)sm_count() ? a.tiles : (int64_t)sm_count();
-  conv_tc_kernel<<<(unsigned)ctas, TC_THREADS, smem, resolve_stream(stream)>>>(mhi, mlo, amap, a);
+  kernel<<<(unsigned)ctas, TC_THREADS, smem, resolve_stream(stream)>>>(mhi, mlo, amap, a);
   MM_LAUNCH_CHECK("mm_conv2d_tc launch");
   return MM_OK;
 }

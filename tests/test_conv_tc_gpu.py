@@ -58,6 +58,8 @@ def run_case(mm, n, c, k, ksz, stride, pad, hw, act=2, residual=None, seed=0):
     (1, 64, 64, 1, 1, 0, 33),     # 1x1
     (1, 48, 80, 3, 1, 1, 17),     # detect class branch width
     (1, 4, 5, 3, 1, 1, 64),       # config-1 channel counts (C padded to 32)
+    (1, 20, 24, 3, 1, 1, 16),     # last channel block: 3 of 4 eight-channel steps
+    (2, 40, 32, 3, 2, 1, 18),     # second channel block holds 8 channels (1 step)
     (1, 128, 144, 1, 1, 0, 12),   # K not a multiple of 16 tile
     (1, 96, 576, 3, 2, 1, 10),    # K > 256: three N tiles
     (3, 256, 256, 3, 1, 1, 7),    # deep layer
