@@ -4,30 +4,33 @@
 // (tap r, tap s, channel c) with channels padded to C_pad (multiple of 32).
 //
 // Persistent CTAs (one per SM) walk a static list of 128-pixel x BN-channel
-// tiles (BN <= 80).  Warp roles:
-//   * warps 0-7 (A producers, two per TMEM lane quarter): copy their 32 pixel
-//     rows x 16 channels of every 32-channel k-block with 16-byte cp.async
-//     into a private 4-deep shared-memory ring that runs ahead across tile
-//     boundaries (zero-fill for padding taps, rows past the end and padded
-//     channels), split each value into a tf32 high part (round to nearest) and
-//     the exact fp32 remainder, and write both planes into a TMEM A stage with
-//     tcgen05.st -- so the MMAs read only the weights from shared memory;
+// tiles (BN <= 80).  A k-block is 32 channels of one tap; a stage holds its A
+// tile (128 pixel rows x 128 B) and the B hi and B lo weight tiles (BN rows x
+// 128 B each, adjacent) in shared memory.  Warp roles:
+//   * warps 0-7 (A producers, two per TMEM lane quarter): in the TMA modes
+//     they read their 32 rows x 16 channels of the A tile and write the exact
+//     remainder x - tf32(x) into a TMEM lo stage with tcgen05.st; in the
+//     gather mode they first fetch the tile with 16-byte cp.async (zero-fill
+//     for padding taps, rows past the end and padded channels);
 //   * warp 8 (TMA): prepacked [K_pad][R*S*C_pad] weight hi/lo planes, one 2-D
-//     tiled load each per stage into this CTA's shared memory;
-//   * warps 9, 10, 11 (MMA issue, one thread each): A_hi*B_hi, A_hi*B_lo and
-//     A_lo*B_hi, four tcgen05.mma.kind::tf32 per k-block each, into separate
-//     TMEM accumulators.  Three issuing threads overlap the per-instruction
-//     issue latency that bounds a single issuer at small N.  The hi*hi sum
-//     alternates between two period buffers handed over every `period`
-//     k-blocks; the two cross terms (~2^-11 of the result) accumulate a whole
-//     tile each;
-//   * warps 12-19 (accumulator, two per lane quarter): add each finished
-//     hi*hi period into an fp32 total held in registers with round-to-nearest
-//     adds -- the tensor core's own accumulation rounds toward zero, so long
-//     reductions inside TMEM drift by ~K * 2^-24 -- then add the cross terms
-//     and apply bias (staged in shared memory), activation and the optional
-//     residual, and store the NHWC output (possibly a channel slice of a
-//     concat buffer).  The epilogue of one tile overlaps the MMAs of the next.
+//     tiled load each per stage, and the A tile in the TMA modes;
+//   * warp 9 (hi MMAs): A (fp32 in shared memory, which the tensor core reads
+//     as tf32 -- the high part of the split) times [B hi | B lo] as one
+//     N = 2 BN tcgen05.mma.kind::tf32 per 8 channels, so each A slice is read
+//     from shared memory once for both products.  The [hi*hi | hi*lo] sums
+//     alternate between two period buffers handed over every `period` k-blocks;
+//   * warp 10 (lo MMAs): A lo (TMEM) times B hi, accumulated over a whole tile
+//     (~2^-11 of the result);
+//   * warps 11-18 (accumulator, two per lane quarter): add each finished
+//     period's hi*hi + hi*lo into an fp32 total held in registers with
+//     round-to-nearest adds -- the tensor core's own accumulation rounds
+//     toward zero, so long reductions inside TMEM drift by ~K * 2^-24 -- then
+//     add the lo*hi sum and apply bias (staged in shared memory), activation
+//     and the optional residual, and store the NHWC output (possibly a channel
+//     slice of a concat buffer).  The epilogue of one tile overlaps the MMAs
+//     of the next.
+// The MMA issue warps and the TMA warp run their loops and waits on all 32
+// lanes (warp-uniform state); one elected lane issues.
 //
 // Stage and phase counters advance incrementally (no divisions in the
 // per-k-block paths), and per-row input offsets are computed once per tile.
@@ -293,10 +296,10 @@ struct TcArgs {
   int64_t mtiles; // pixel tiles
   int64_t tiles;  // mtiles * n_tiles
   int stages;     // pipeline depth (A/B shared-memory stages == TMEM lo stages)
-  int xbuf;       // cross-term accumulator sets (2: the next tile's cross terms overlap the epilogue)
+  int xbuf;       // lo*hi tile-sum buffers (2: the next tile's sum overlaps the epilogue)
   int epi_groups; // 2: two groups of 4 epilogue warps take alternate tiles (needs one hi*hi
                   // period per tile, xbuf == 2 and bn <= 48, so each group owns its buffers)
-  int period;     // k-blocks of hi*hi products accumulated in TMEM before promotion
+  int period;     // k-blocks of hi products accumulated in TMEM before promotion
   int act, res_before_act;
   int vec_store;  // output rows 16-byte aligned: float4 stores
   int res_vec;    // residual rows 16-byte aligned: float4 loads
@@ -312,17 +315,16 @@ constexpr int TC_A_RECT = 2;    // one 4-D TMA load of a th x tw output-pixel re
 // Warp roles of the persistent kernel.
 constexpr int TC_A_WARPS = 8;      // warps 0-7: A producers (2 per TMEM lane quarter)
 constexpr int TC_WARP_TMA = 8;     // warp 8: TMA (weights; A in the TMA modes)
-constexpr int TC_WARP_HH = 9;      // warp 9: hi*hi MMA issue + TMEM owner
-constexpr int TC_WARP_HL = 10;     // warp 10: hi*lo MMA issue
-constexpr int TC_WARP_LH = 11;     // warp 11: lo*hi MMA issue
-constexpr int TC_WARP_EPI = 12;    // warps 12-19: promotion + epilogue (2 per lane quarter)
+constexpr int TC_WARP_HI = 9;      // warp 9: A hi * [B hi | B lo] MMA issue + TMEM owner
+constexpr int TC_WARP_LO = 10;     // warp 10: A lo * B hi MMA issue
+constexpr int TC_WARP_EPI = 11;    // warps 11-18: promotion + epilogue (2 per lane quarter)
 constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_EPI_CHUNKS = 3;   // 16-column chunks per epilogue warp (bn <= 96)
 constexpr int TC_THREADS = (TC_WARP_EPI + TC_EPI_WARPS) * 32;
 constexpr uint32_t TC_TMEM_COLS = 512;
 constexpr int TC_LO_COLS = 32;     // TMEM columns per lo stage
 constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 4;  // one A tile: 128 rows x 128 B
-constexpr int TC_MAX_BN = 80;      // N tile limit (4 accumulators of bn columns + lo stages)
+constexpr int TC_MAX_BN = 80;      // N tile limit (6 accumulator widths of bn columns + lo stages)
 constexpr int TC_MAX_STAGES = 8;
 constexpr int TC_MAX_BIAS = 2048;  // output channels whose bias is staged in shared memory
 
@@ -392,7 +394,8 @@ struct TcSmem {
     return l;
   }
   // mbarriers: full_x[S], full_b[S], full_lo[S], empty[S], hh_full[2],
-  // hh_free[2], cross_full[2], cross_free[2], drain[3]; then the TMEM slot.
+  // hh_free[2], cross_full[2], cross_free[2], drain[3] (two used); then the
+  // TMEM slot.
   __host__ __device__ int n_bars() const { return 4 * stages + 11; }
   __host__ __device__ size_t bytes() const { return 1024 + bars + (size_t)n_bars() * 8 + 16; }
 };
@@ -445,15 +448,34 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int j) {
   return (uint32_t)(row * 128 + ((j ^ (row & 7)) << 4));
 }
 
-// One MMA issuer.  ROLE 0 (hi*hi) and ROLE 1 (hi*lo) read the A tile straight
-// from shared memory: for fp32 data the tensor core uses the value truncated
-// to tf32, which is the high part of the split.  ROLE 2 (lo*hi) reads the
-// exact remainder x - trunc(x) that the producer warps wrote into a TMEM lo
-// stage.  ROLE 0 rotates between two period buffers that the promotion warps
-// fold into the fp32 total every `period` k-blocks; ROLE 1 and ROLE 2
-// accumulate a whole tile into one buffer each -- their partial sums are
-// ~2^-11 of the result, so the tensor core's round-toward-zero accumulation
-// leaves no measurable drift there.
+// The lowest active lane of the warp: the one thread that issues a warp's
+// MMAs and commits (tcgen05.commit tracks the MMAs of the issuing thread).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t leader;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 l;\n\t"
+      "elect.sync l|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(leader));
+  return leader != 0;
+}
+
+// Bounded wait by a whole warp, with one outcome for all lanes.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int code) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, code));
+}
+
+// One MMA issuer warp.  ROLE 0 (hi) reads the A tile straight from shared
+// memory -- for fp32 data the tensor core uses the value truncated to tf32,
+// which is the high part of the split -- and multiplies it by the adjacent
+// B hi and B lo tiles as one N = 2 bn operand, producing [hi*hi | hi*lo] in a
+// period buffer that the promotion warps fold into the fp32 total every
+// `period` k-blocks (two buffers alternate).  ROLE 1 (lo) reads the exact
+// remainder x - trunc(x) that the producer warps wrote into a TMEM lo stage
+// and multiplies it by B hi into a per-tile buffer: its sum is ~2^-11 of the
+// result, so the tensor core's round-toward-zero accumulation leaves no
+// measurable drift there.  All 32 lanes run the loop and the waits (its state
+// stays warp-uniform); one elected lane issues.
 template <int ROLE>
 __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const TcSmem& L,
                                          uint32_t tmem, uint64_t* full_x, uint64_t* full_b,
@@ -462,15 +484,12 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
                                          uint64_t* cross_free, uint64_t* drain) {
   const int S = a.stages, KB = a.kb_total;
   const int NP = (KB + a.period - 1) / a.period;
-  const uint32_t b_bytes = (uint32_t)a.bn * 128;
   const uint32_t acc0 = (uint32_t)(TC_LO_COLS * S);
-  const uint32_t idesc = idesc_tf32(TC_BM, a.bn);
-  // B hi for hi*hi and lo*hi, B lo for hi*lo.
-  const uint32_t b_off = TC_A_BYTES + (ROLE == 1 ? b_bytes : 0u);
-  // cp.async writes the gathered tile through the generic proxy: the hi*hi and
-  // hi*lo MMAs then wait for full_lo, which every producer thread signals only
-  // after a proxy fence that makes its copies visible to the tensor core.
-  uint64_t* full_a = (ROLE == 2 || a.amode == TC_A_GATHER) ? full_lo : full_x;
+  const uint32_t idesc = idesc_tf32(TC_BM, ROLE == 0 ? 2 * a.bn : a.bn);
+  // cp.async writes the gathered tile through the generic proxy: the hi MMAs
+  // then wait for full_lo, which every producer thread signals only after a
+  // proxy fence that makes its copies visible to the tensor core.
+  uint64_t* full_a = (ROLE == 1 || a.amode == TC_A_GATHER) ? full_lo : full_x;
   int64_t pc = 0, tc = 0;
   int st = 0;         // A/B stage of the next k-block
   uint32_t par = 0;   // its fill phase parity
@@ -478,9 +497,9 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
   for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x, ++tc) {
     const int xb = a.xbuf == 2 ? (int)(tc & 1) : 0;
     const uint32_t xpar = (uint32_t)((a.xbuf == 2 ? tc >> 1 : tc) & 1);
-    uint32_t d = tmem + acc0 + (uint32_t)((2 + 2 * xb + (ROLE == 1 ? 0 : 1)) * a.bn);
-    if (ROLE != 0) {
-      if (!mbar_wait(&cross_free[xb], xpar ^ 1u, TC_ERR_WAIT_ACC)) {
+    uint32_t d = tmem + acc0 + (uint32_t)((4 + xb) * a.bn);
+    if (ROLE == 1) {
+      if (!warp_wait(&cross_free[xb], xpar ^ 1u, TC_ERR_WAIT_ACC)) {
         alive = false;
         break;
       }
@@ -489,50 +508,58 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
     for (int p = 0; p < NP && alive; ++p) {
       if (ROLE == 0) {
         const int b = (int)(pc & 1);
-        if (!mbar_wait(&hh_free[b], (uint32_t)((pc >> 1) & 1) ^ 1u, TC_ERR_WAIT_ACC)) {
+        if (!warp_wait(&hh_free[b], (uint32_t)((pc >> 1) & 1) ^ 1u, TC_ERR_WAIT_ACC)) {
           alive = false;
           break;
         }
         tc_fence_after();
-        d = tmem + acc0 + (uint32_t)(b * a.bn);
+        d = tmem + acc0 + (uint32_t)(b * 2 * a.bn);
       }
       const int kb_begin = p * a.period;
       const int kb_end = min(KB, kb_begin + a.period);
       for (int kb = kb_begin; kb < kb_end; ++kb) {
-        if (!mbar_wait(&full_a[st], par, TC_ERR_WAIT_A) ||
-            !mbar_wait(&full_b[st], par, TC_ERR_WAIT_B)) {
+        if (!warp_wait(&full_a[st], par, TC_ERR_WAIT_A) ||
+            !warp_wait(&full_b[st], par, TC_ERR_WAIT_B)) {
           alive = false;
           break;
         }
         tc_fence_after();
         const uint32_t stage = smem_addr(smem + (size_t)st * L.stage_bytes);
-        const uint32_t bs = stage + b_off;
+        const uint32_t bs = stage + TC_A_BYTES;  // B hi, then B lo (bn rows each)
         const bool first = ROLE == 0 ? kb == kb_begin : kb == 0;
+        if (elect_one()) {
 #pragma unroll
-        for (int k = 0; k < TC_BK / 8; ++k) {
-          const uint32_t acc = (first && k == 0) ? 0u : 1u;
-          if (ROLE == 2)
-            mma_tf32_ts(d, tmem + (uint32_t)(st * TC_LO_COLS + 8 * k), smem_desc_sw128(bs + 32 * k),
-                        idesc, acc);
-          else
-            mma_tf32(d, smem_desc_sw128(stage + 32 * k), smem_desc_sw128(bs + 32 * k), idesc, acc);
+          for (int k = 0; k < TC_BK / 8; ++k) {
+            const uint32_t acc = (first && k == 0) ? 0u : 1u;
+            if (ROLE == 1)
+              mma_tf32_ts(d, tmem + (uint32_t)(st * TC_LO_COLS + 8 * k),
+                          smem_desc_sw128(bs + 32 * k), idesc, acc);
+            else
+              mma_tf32(d, smem_desc_sw128(stage + 32 * k), smem_desc_sw128(bs + 32 * k), idesc, acc);
+          }
+          mma_commit(&empty[st]);
         }
-        mma_commit(&empty[st]);
+        __syncwarp();
         if (++st == S) {
           st = 0;
           par ^= 1u;
         }
       }
       if (ROLE == 0 && alive) {
-        mma_commit(&hh_full[pc & 1]);  // arrives once the period's MMAs have completed
+        if (elect_one()) mma_commit(&hh_full[pc & 1]);  // arrives once the period's MMAs complete
+        __syncwarp();
         ++pc;
       }
     }
-    if (ROLE != 0 && alive) mma_commit(&cross_full[xb]);
+    if (ROLE == 1 && alive) {
+      if (elect_one()) mma_commit(&cross_full[xb]);
+      __syncwarp();
+    }
   }
-  if (!alive || tc_error_raised()) {
-    // Error path: no MMA of this thread may still write TMEM when it is freed.
-    mma_commit(&drain[ROLE]);
+  if (__any_sync(0xffffffffu, !alive || tc_error_raised())) {
+    // Error path: no MMA of this warp may still write TMEM when it is freed.
+    if (elect_one()) mma_commit(&drain[ROLE]);
+    __syncwarp();
     mbar_wait(&drain[ROLE], 0u, TC_ERR_WAIT_ACC);
   }
 }
@@ -638,9 +665,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* full_b = bars + S;            // S: B tiles (TMA transaction bytes)
   uint64_t* full_lo = bars + 2 * S;       // S: lo plane in TMEM (one arrival per producer thread)
   uint64_t* empty = bars + 3 * S;         // S: one commit per issuer frees the stage
-  uint64_t* hh_full = bars + 4 * S;       // 2: hi*hi period complete in TMEM
+  uint64_t* hh_full = bars + 4 * S;       // 2: [hi*hi | hi*lo] period complete in TMEM
   uint64_t* hh_free = bars + 4 * S + 2;   // 2: one arrival per promotion thread
-  uint64_t* cross_full = bars + 4 * S + 4;  // 2: hi*lo and lo*hi tile sums complete
+  uint64_t* cross_full = bars + 4 * S + 4;  // 2: lo*hi tile sum complete
   uint64_t* cross_free = bars + 4 * S + 6;  // 2: one arrival per epilogue thread
   uint64_t* drain = bars + 4 * S + 8;       // 3: issuer error paths wait for their MMAs
   uint32_t* tmem_slot = (uint32_t*)(bars + L.n_bars());
@@ -658,20 +685,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&full_x[i], a.amode == TC_A_GATHER ? TC_A_WARPS * 32 : 1);
       mbar_init(&full_b[i], 1);
       mbar_init(&full_lo[i], TC_A_WARPS * 32);
-      mbar_init(&empty[i], 3);
+      mbar_init(&empty[i], 2);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&hh_full[i], 1);
       mbar_init(&hh_free[i], 32 * (a.epi_groups == 2 ? TC_EPI_WARPS / 2 : TC_EPI_WARPS));
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&cross_full[i], 2);
+      mbar_init(&cross_full[i], 1);
       mbar_init(&cross_free[i], 32 * (a.epi_groups == 2 ? TC_EPI_WARPS / 2 : TC_EPI_WARPS));
     }
     for (int i = 0; i < 3; ++i) mbar_init(&drain[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == TC_WARP_HH) {
+  if (warp == TC_WARP_HI) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_slot)),
                  "r"(TC_TMEM_COLS)
@@ -683,9 +710,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: lo stages at [32 s, 32 s + 32); from acc0 = 32 S the hi*hi
-  // period buffers [acc0, acc0 + 2 bn), then xbuf cross-term sets of 2 bn
-  // columns (hi*lo tile sum, then lo*hi tile sum).
+  // TMEM columns: lo stages at [32 s, 32 s + 32); from acc0 = 32 S two period
+  // buffers of 2 bn columns ([hi*hi | hi*lo], [acc0, acc0 + 4 bn)), then xbuf
+  // lo*hi tile sums of bn columns.
   const uint32_t acc0 = (uint32_t)(TC_LO_COLS * S);
   const int KB = a.kb_total;
   const int NP = (KB + a.period - 1) / a.period;
@@ -840,7 +867,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else if (warp == TC_WARP_TMA) {
     // ---------------- TMA: weights, and the A tile in the TMA modes ----------------
-    if (lane == 0) {
+    // The whole warp runs the loop and the waits; one elected lane issues.
+    {
       int64_t g = 0;
       int st = 0;
       uint32_t par = 0;
@@ -850,23 +878,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int n0 = (int)(tile % a.n_tiles) * a.bn;
         int kr = 0, ks = 0, cbk = 0;
         for (int kb = 0; kb < KB; ++kb, ++g) {
-          if (!mbar_wait(&empty[st], par ^ 1u, TC_ERR_WAIT_EMPTY)) {
+          if (!warp_wait(&empty[st], par ^ 1u, TC_ERR_WAIT_EMPTY)) {
             alive = false;
             break;
           }
-          uint8_t* stage = smem + (size_t)st * L.stage_bytes;
-          if (a.amode == TC_A_FLAT) {
-            mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES);
-            tma_load_2d(stage, &amap, &full_x[st], cbk * TC_BK, t.m0);
-          } else if (a.amode == TC_A_RECT) {
-            // Taps outside the image read as zero (TMA out-of-bounds fill).
-            mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES);
-            tma_load_4d(stage, &amap, &full_x[st], cbk * TC_BK, t.ow0 * a.sw - a.pw + ks * a.dw,
-                        t.oh0 * a.sh - a.ph + kr * a.dh, t.n);
+          if (elect_one()) {
+            uint8_t* stage = smem + (size_t)st * L.stage_bytes;
+            if (a.amode == TC_A_FLAT) {
+              mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES);
+              tma_load_2d(stage, &amap, &full_x[st], cbk * TC_BK, t.m0);
+            } else if (a.amode == TC_A_RECT) {
+              // Taps outside the image read as zero (TMA out-of-bounds fill).
+              mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES);
+              tma_load_4d(stage, &amap, &full_x[st], cbk * TC_BK, t.ow0 * a.sw - a.pw + ks * a.dw,
+                          t.oh0 * a.sh - a.ph + kr * a.dh, t.n);
+            }
+            mbar_arrive_expect_tx(&full_b[st], 2 * b_bytes);
+            tma_load_2d(stage + TC_A_BYTES, &wmap_hi, &full_b[st], kb * TC_BK, n0);
+            tma_load_2d(stage + TC_A_BYTES + b_bytes, &wmap_lo, &full_b[st], kb * TC_BK, n0);
           }
-          mbar_arrive_expect_tx(&full_b[st], 2 * b_bytes);
-          tma_load_2d(stage + TC_A_BYTES, &wmap_hi, &full_b[st], kb * TC_BK, n0);
-          tma_load_2d(stage + TC_A_BYTES + b_bytes, &wmap_lo, &full_b[st], kb * TC_BK, n0);
+          __syncwarp();
           if (++st == S) {
             st = 0;
             par ^= 1u;
@@ -887,18 +918,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (a.amode != TC_A_GATHER) mbar_wait(&full_x[k % S], kp, TC_ERR_WAIT_A);
       }
     }
-  } else if (warp == TC_WARP_HH) {
-    if (lane == 0)
-      tc_issue<0>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
-                  cross_free, drain);
-  } else if (warp == TC_WARP_HL) {
-    if (lane == 0)
-      tc_issue<1>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
-                  cross_free, drain);
-  } else if (warp == TC_WARP_LH) {
-    if (lane == 0)
-      tc_issue<2>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
-                  cross_free, drain);
+  } else if (warp == TC_WARP_HI) {
+    tc_issue<0>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
+                cross_free, drain);
+  } else if (warp == TC_WARP_LO) {
+    tc_issue<1>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
+                cross_free, drain);
   } else if (warp >= TC_WARP_EPI) {
     // ---------------- promotion (fp32 RN adds) + epilogue ----------------
     // Two warps per TMEM lane quarter; warp half h owns the 16-column chunks
@@ -921,10 +946,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int64_t tile = blockIdx.x + tc * gridDim.x; tile < a.tiles && alive;
          tile += tstep * (int64_t)gridDim.x, tc += tstep) {
       float tot[TC_EPI_CHUNKS * 16];
-      int64_t pc = tc * NP;  // this tile's first hi*hi period
+      int64_t pc = tc * NP;  // this tile's first period
       const int xb = a.xbuf == 2 ? (int)(tc & 1) : 0;
       const uint32_t xpar = (uint32_t)((a.xbuf == 2 ? tc >> 1 : tc) & 1);
-      const uint32_t cross = lane_base + acc0 + (uint32_t)((2 + 2 * xb) * a.bn);
+      const uint32_t cross = lane_base + acc0 + (uint32_t)((4 + xb) * a.bn);
       for (int p = 0; p < NP; ++p, ++pc) {
         const int b = (int)(pc & 1);  // (in group mode NP == 1: buffer = tile parity = group)
         if (!mbar_wait(&hh_full[b], (uint32_t)((pc >> 1) & 1), TC_ERR_WAIT_ACC)) {
@@ -932,17 +957,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t buf = lane_base + acc0 + (uint32_t)(b * a.bn);
+        const uint32_t buf = lane_base + acc0 + (uint32_t)(b * 2 * a.bn);
 #pragma unroll
         for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
           const int c = h + cstep * j;
           if (c < nchunk) {
-            uint32_t v[16];
-            tmem_ld16_nowait(buf + (uint32_t)(16 * c), v);
+            uint32_t u[16], w[16];  // hi*hi, hi*lo
+            tmem_ld16_nowait(buf + (uint32_t)(16 * c), u);
+            tmem_ld16_nowait(buf + (uint32_t)(a.bn + 16 * c), w);
             tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              tot[16 * j + e] = p == 0 ? __uint_as_float(v[e]) : __fadd_rn(tot[16 * j + e], __uint_as_float(v[e]));
+            for (int e = 0; e < 16; ++e) {
+              const float v = __fadd_rn(__uint_as_float(u[e]), __uint_as_float(w[e]));
+              tot[16 * j + e] = p == 0 ? v : __fadd_rn(tot[16 * j + e], v);
+            }
           }
         }
         tc_fence_before();
@@ -958,14 +986,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
         const int c = h + cstep * j;
         if (c < nchunk) {
-          uint32_t u[16], w[16];
+          uint32_t u[16];  // lo*hi
           tmem_ld16_nowait(cross + (uint32_t)(16 * c), u);
-          tmem_ld16_nowait(cross + (uint32_t)(a.bn + 16 * c), w);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            tot[16 * j + e] =
-                __fadd_rn(tot[16 * j + e], __fadd_rn(__uint_as_float(u[e]), __uint_as_float(w[e])));
+          for (int e = 0; e < 16; ++e) tot[16 * j + e] = __fadd_rn(tot[16 * j + e], __uint_as_float(u[e]));
         }
       }
       tc_fence_before();
@@ -985,7 +1010,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == TC_WARP_HH) {
+  if (warp == TC_WARP_HI) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(TC_TMEM_COLS)
@@ -1258,8 +1283,8 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   a.div_ntw = make_fastdiv((uint32_t)a.ntw);
   a.mtiles = a.amode == TC_A_RECT ? n * (int64_t)a.ntw * a.nth : (m_total + TC_BM - 1) / TC_BM;
   a.tiles = a.mtiles * a.n_tiles;
-  // Stages: TMEM holds S lo stages of 32 columns plus four accumulators of bn
-  // columns (two hi*hi period buffers, the hi*lo and lo*hi tile sums); shared
+  // Stages: TMEM holds S lo stages of 32 columns, two [hi*hi | hi*lo] period
+  // buffers of 2 bn columns and xbuf lo*hi tile sums of bn columns; shared
   // memory holds S (A + B hi + B lo) stages, the bias and the barriers.
   int dev = 0;
   MM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
@@ -1269,7 +1294,7 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   int stages = 0;
   for (int xbuf = 2; xbuf >= 1 && stages == 0; --xbuf) {
     for (int st = TC_MAX_STAGES; st >= (xbuf == 2 ? 4 : 3); --st) {
-      if (TC_LO_COLS * st + (2 + 2 * xbuf) * a.bn <= (int)TC_TMEM_COLS &&
+      if (TC_LO_COLS * st + (4 + xbuf) * a.bn <= (int)TC_TMEM_COLS &&
           TcSmem::make(a.bn, st, k_out).bytes() <= smem_limit) {
         stages = st;
         a.xbuf = xbuf;
