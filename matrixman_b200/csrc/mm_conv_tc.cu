@@ -518,8 +518,10 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
       const int kb_begin = p * a.period;
       const int kb_end = min(KB, kb_begin + a.period);
       for (int kb = kb_begin; kb < kb_end; ++kb) {
+        // TMA modes: full_x carries the weights too (the lo issuer's full_lo
+        // follows the producers' wait on full_x).
         if (!warp_wait(&full_a[st], par, TC_ERR_WAIT_A) ||
-            !warp_wait(&full_b[st], par, TC_ERR_WAIT_B)) {
+            (a.amode == TC_A_GATHER && !warp_wait(&full_b[st], par, TC_ERR_WAIT_B))) {
           alive = false;
           break;
         }
@@ -539,7 +541,6 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
           }
           mma_commit(&empty[st]);
         }
-        __syncwarp();
         if (++st == S) {
           st = 0;
           par ^= 1u;
@@ -547,13 +548,11 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
       }
       if (ROLE == 0 && alive) {
         if (elect_one()) mma_commit(&hh_full[pc & 1]);  // arrives once the period's MMAs complete
-        __syncwarp();
         ++pc;
       }
     }
     if (ROLE == 1 && alive) {
       if (elect_one()) mma_commit(&cross_full[xb]);
-      __syncwarp();
     }
   }
   if (__any_sync(0xffffffffu, !alive || tc_error_raised())) {
@@ -661,8 +660,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   float* bias_s = (float*)(smem + L.bias);
   const uint32_t b_bytes = (uint32_t)a.bn * 128;
   uint64_t* bars = (uint64_t*)(smem + L.bars);
-  uint64_t* full_x = bars;                // S: A tile in shared memory
-  uint64_t* full_b = bars + S;            // S: B tiles (TMA transaction bytes)
+  uint64_t* full_x = bars;                // S: A tile (and, in the TMA modes, the B tiles)
+  uint64_t* full_b = bars + S;            // S: B tiles in the gather mode (TMA transaction bytes)
   uint64_t* full_lo = bars + 2 * S;       // S: lo plane in TMEM (one arrival per producer thread)
   uint64_t* empty = bars + 3 * S;         // S: one commit per issuer frees the stage
   uint64_t* hh_full = bars + 4 * S;       // 2: [hi*hi | hi*lo] period complete in TMEM
@@ -884,20 +883,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           if (elect_one()) {
             uint8_t* stage = smem + (size_t)st * L.stage_bytes;
+            // TMA modes: A and both weight tiles complete on full_x; gather
+            // mode: the weights on full_b (A arrives by the producers' cp.async).
+            uint64_t* bbar = a.amode == TC_A_GATHER ? &full_b[st] : &full_x[st];
             if (a.amode == TC_A_FLAT) {
-              mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES);
+              mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES + 2 * b_bytes);
               tma_load_2d(stage, &amap, &full_x[st], cbk * TC_BK, t.m0);
             } else if (a.amode == TC_A_RECT) {
               // Taps outside the image read as zero (TMA out-of-bounds fill).
-              mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES);
+              mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES + 2 * b_bytes);
               tma_load_4d(stage, &amap, &full_x[st], cbk * TC_BK, t.ow0 * a.sw - a.pw + ks * a.dw,
                           t.oh0 * a.sh - a.ph + kr * a.dh, t.n);
+            } else {
+              mbar_arrive_expect_tx(&full_b[st], 2 * b_bytes);
             }
-            mbar_arrive_expect_tx(&full_b[st], 2 * b_bytes);
-            tma_load_2d(stage + TC_A_BYTES, &wmap_hi, &full_b[st], kb * TC_BK, n0);
-            tma_load_2d(stage + TC_A_BYTES + b_bytes, &wmap_lo, &full_b[st], kb * TC_BK, n0);
+            tma_load_2d(stage + TC_A_BYTES, &wmap_hi, bbar, kb * TC_BK, n0);
+            tma_load_2d(stage + TC_A_BYTES + b_bytes, &wmap_lo, bbar, kb * TC_BK, n0);
           }
-          __syncwarp();
           if (++st == S) {
             st = 0;
             par ^= 1u;
@@ -914,8 +916,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // Bulk copies must not outlive the CTA's shared memory.
       for (int64_t k = (g > S ? g - S : 0); k < g; ++k) {
         const uint32_t kp = (uint32_t)((k / S) & 1);
-        mbar_wait(&full_b[k % S], kp, TC_ERR_WAIT_B);
-        if (a.amode != TC_A_GATHER) mbar_wait(&full_x[k % S], kp, TC_ERR_WAIT_A);
+        if (a.amode == TC_A_GATHER)
+          mbar_wait(&full_b[k % S], kp, TC_ERR_WAIT_B);
+        else
+          mbar_wait(&full_x[k % S], kp, TC_ERR_WAIT_A);
       }
     }
   } else if (warp == TC_WARP_HI) {

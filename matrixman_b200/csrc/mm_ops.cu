@@ -10,6 +10,7 @@
 // grid-strided.
 #include <cuda_runtime.h>
 #include <math.h>
+#include <algorithm>
 #include <stdint.h>
 
 #include <string>
@@ -526,6 +527,73 @@ __global__ void yolo_decode_kernel(DecodeArgs a) {
   }
 }
 
+// The same decode for the layout the prepared YOLO head writes: NHWC feature
+// rows (channel stride 1, 16-byte aligned), 16 distribution bins, nc a
+// multiple of 4.  One thread per anchor, blockIdx.y = image; a warp covers 32
+// consecutive pixels of one level, i.e. one contiguous block of rows, and each
+// phase issues its float4 loads back to back so every line is fetched once.
+// The arithmetic is the generic kernel's, in the same order (same results).
+__global__ void __launch_bounds__(128) yolo_decode_rows_kernel(DecodeArgs a) {
+  const int an = (int)(blockIdx.x * blockDim.x + threadIdx.x);
+  if (an >= (int)a.anchors) return;
+  int l = 0;
+  while (l + 1 < a.nlevels && an >= (int)a.lv[l + 1].anchor0) ++l;
+  const DecodeLevel& L = a.lv[l];
+  const int local = an - (int)L.anchor0;
+  const int yy = local / (int)L.w, xx = local - yy * (int)L.w;
+  const float ax = (float)xx + 0.5f, ay = (float)yy + 0.5f;
+  for (int64_t n = blockIdx.y; n < a.batch; n += gridDim.y) {
+    const float4* f = reinterpret_cast<const float4*>(L.base + n * L.sn + yy * L.sh + xx * L.sw);
+    float4 v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __ldg(f + j);
+    float dist[4];
+#pragma unroll
+    for (int side = 0; side < 4; ++side) {
+      const float lg[16] = {v[4 * side].x,     v[4 * side].y,     v[4 * side].z,     v[4 * side].w,
+                            v[4 * side + 1].x, v[4 * side + 1].y, v[4 * side + 1].z, v[4 * side + 1].w,
+                            v[4 * side + 2].x, v[4 * side + 2].y, v[4 * side + 2].z, v[4 * side + 2].w,
+                            v[4 * side + 3].x, v[4 * side + 3].y, v[4 * side + 3].z, v[4 * side + 3].w};
+      float m = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) m = fmaxf(m, lg[k]);
+      float s = 0.f, e = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        float p = expf(lg[k] - m);
+        s += p;
+        e += p * (float)k;
+      }
+      dist[side] = e / s;
+    }
+    float x1 = ax - dist[0], y1 = ay - dist[1];
+    float x2 = ax + dist[2], y2 = ay + dist[3];
+    float* o = a.out + n * a.on + (int64_t)an * a.oa;
+    o[0 * a.oc] = (x1 + x2) * 0.5f * L.stride;
+    o[1 * a.oc] = (y1 + y2) * 0.5f * L.stride;
+    o[2 * a.oc] = (x2 - x1) * L.stride;
+    o[3 * a.oc] = (y2 - y1) * L.stride;
+    const float4* cl = f + 16;
+    for (int k4 = 0; k4 < a.nc / 4; k4 += 5) {
+      float4 c[5];
+      const int cnt = min(5, a.nc / 4 - k4);
+#pragma unroll
+      for (int j = 0; j < 5; ++j)
+        if (j < cnt) c[j] = __ldg(cl + k4 + j);
+#pragma unroll
+      for (int j = 0; j < 5; ++j) {
+        if (j < cnt) {
+          float* oc = o + (int64_t)(4 + 4 * (k4 + j)) * a.oc;
+          oc[0] = 1.0f / (1.0f + expf(-c[j].x));
+          oc[a.oc] = 1.0f / (1.0f + expf(-c[j].y));
+          oc[2 * a.oc] = 1.0f / (1.0f + expf(-c[j].z));
+          oc[3 * a.oc] = 1.0f / (1.0f + expf(-c[j].w));
+        }
+      }
+    }
+  }
+}
+
 // tf32 split: hi = x with the 13 low mantissa bits cleared, lo = x - hi (exact).
 __global__ void tf32_split_kernel(const float* __restrict__ src, float* __restrict__ hi,
                                   float* __restrict__ lo, int64_t n) {
@@ -1034,6 +1102,18 @@ extern "C" int mm_yolo_decode(const mm_tensor_t* const* feats, const float* stri
   int64_t total = a.batch * anchors;
   if (total == 0) return MM_OK;
   cudaStream_t s = resolve_stream(stream);
+  bool rows = reg_max == 16 && nc % 4 == 0 && anchors < 0x7fffffffLL;
+  for (int l = 0; l < nlevels && rows; ++l) {
+    const DecodeLevel& L = a.lv[l];
+    rows = L.sc == 1 && ((uintptr_t)L.base & 15) == 0 && L.sw % 4 == 0 && L.sh % 4 == 0 &&
+           L.sn % 4 == 0;
+  }
+  if (rows) {
+    const dim3 grid((unsigned)((anchors + 127) / 128), (unsigned)std::min<int64_t>(a.batch, 65535));
+    yolo_decode_rows_kernel<<<grid, 128, 0, s>>>(a);
+    MM_LAUNCH_CHECK("mm_yolo_decode launch");
+    return MM_OK;
+  }
   yolo_decode_kernel<<<grid_for(total, 128, (int64_t)sm_count() * 16), 128, 0, s>>>(a);
   MM_LAUNCH_CHECK("mm_yolo_decode launch");
   return MM_OK;

@@ -72,6 +72,7 @@ def test_config1_conv(mm):
     (8, 16, 3, 2, 1, 1, 8, 16, 1),
     (12, 24, 5, 1, 2, 1, 3, 11, 2),
     (3, 64, 7, 2, 3, 1, 1, 56, 1),
+    (3, 20, 3, 2, 1, 1, 1, 31, 1),   # stem with a partial second 16-channel group
 ])
 def test_conv_shapes_nchw_and_nhwc(mm, c, k, ksz, stride, pad, dil, groups, hw, n):
     g = gen(c * 100 + k)
@@ -296,6 +297,7 @@ def test_batch_norm_eval(mm, golden):
 @pytest.mark.parametrize("nc,hw,batch,layout", [
     (80, (8, 4, 2), 3, "nhwc"),   # 84 anchors per image: 32-anchor chunks straddle levels and images
     (5, (6, 3), 2, "nchw"),       # generic strides, small class count
+    (12, (5, 3), 2, "nhwc"),      # row kernel with a partial group of class loads
 ])
 def test_yolo_decode_matches_oracle(mm, nc, hw, batch, layout):
     import ctypes
