@@ -302,6 +302,8 @@ struct TcArgs {
   int period;     // k-blocks of hi products accumulated in TMEM before promotion
   int act, res_before_act;
   int vec_store;  // output rows 16-byte aligned: float4 stores
+  int stg_chunks; // > 0: the epilogue stages rows in shared memory and writes them with TMA
+                  // stores (this many 16-channel chunks per epilogue warp); 0: direct stores
   int res_vec;    // residual rows 16-byte aligned: float4 loads
   FastDiv div_ow, div_oh, div_img, div_ntw;  // output width, height; rectangles per image, per row
 };
@@ -378,18 +380,48 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// TMA stores of a staged box (bulk-group completion), the group commit and the
+// waits for this thread's groups: `.read` returns once the source shared
+// memory may be reused, the plain form once the global writes are done.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y,
+                                             int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Epilogue staging: each epilogue warp owns stg_chunks boxes of 32 rows x 16
+// channels (64-byte rows, 64-byte swizzle: 16-byte chunk c of row r sits at
+// chunk c ^ ((r >> 1) & 3), which spreads a warp's row writes over all banks).
+constexpr uint32_t TC_STG_BOX = 32 * 64;
+
 // Shared-memory layout of one CTA (offsets from the 1024-aligned base).  A
 // stage holds the A tile (128 pixel rows x 128 B, 128-byte swizzle) and the B
 // hi and lo tiles (bn rows x 128 B each); every stage offset is a multiple of
 // 1024 bytes, as the swizzled layout requires.
 struct TcSmem {
-  uint32_t stage_bytes, bias, bars;
+  uint32_t stage_bytes, stg, bias, bars;
   int stages;
-  __host__ __device__ static TcSmem make(int bn, int stages, int kout) {
+  __host__ __device__ static TcSmem make(int bn, int stages, int kout, int stg_chunks) {
     TcSmem l;
     l.stages = stages;
     l.stage_bytes = TC_A_BYTES + 2u * (uint32_t)bn * 128u;
-    l.bias = (uint32_t)stages * l.stage_bytes;           // kout floats, 16-byte padded
+    l.stg = (uint32_t)stages * l.stage_bytes;           // epilogue staging (1024-aligned)
+    l.bias = l.stg + (uint32_t)TC_EPI_WARPS * (uint32_t)stg_chunks * TC_STG_BOX;  // kout floats, 16-byte padded
     l.bars = l.bias + (((uint32_t)kout * 4u + 15u) & ~15u);
     return l;
   }
@@ -645,6 +677,57 @@ __device__ __forceinline__ void tc_finish_row(const TcArgs& a, float (&tot)[TC_E
   tc_finish_chunk<ACT, RM, 2>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);
 }
 
+// The same epilogue arithmetic into this warp's staging box J (row r of 32)
+// instead of global memory.  Channels past kout get no bias or residual; the
+// TMA store clips them.  `rrow` is null for rows outside the output (the
+// store clips those rows too).
+template <int ACT, int RM, int J>
+__device__ __forceinline__ void tc_stage_chunk(const TcArgs& a, float (&tot)[TC_EPI_CHUNKS * 16],
+                                               int h, int nchunk, int n0, const float* bias_s,
+                                               const float* rrow, uint8_t* stg, int r) {
+  const int c = a.epi_groups == 2 ? J : h + 2 * J;
+  const int cb0 = n0 + 16 * c;
+  if (c >= nchunk || cb0 >= a.kout) return;
+  const bool full = cb0 + 16 <= a.kout;
+  float rv[16];
+  if (RM != 0) {
+    if (rrow != nullptr && full && a.res_vec) {
+#pragma unroll
+      for (int v4 = 0; v4 < 4; ++v4) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(rrow + cb0) + v4);
+        rv[4 * v4] = t.x; rv[4 * v4 + 1] = t.y; rv[4 * v4 + 2] = t.z; rv[4 * v4 + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) rv[e] = (rrow != nullptr && cb0 + e < a.kout) ? __ldg(rrow + cb0 + e) : 0.f;
+    }
+  }
+  uint8_t* row = stg + J * TC_STG_BOX + r * 64;
+#pragma unroll
+  for (int v4 = 0; v4 < 4; ++v4) {
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * v4 + e;
+      float val = tot[16 * J + i] + (full || cb0 + i < a.kout ? bias_s[cb0 + i] : 0.f);
+      if (RM == 1) val += rv[i];
+      val = tc_act_t<ACT>(val);
+      if (RM == 2) val += rv[i];
+      o[e] = val;
+    }
+    *reinterpret_cast<float4*>(row + ((v4 ^ ((r >> 1) & 3)) << 4)) = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int ACT, int RM>
+__device__ __forceinline__ void tc_stage_row(const TcArgs& a, float (&tot)[TC_EPI_CHUNKS * 16],
+                                             int h, int nchunk, int n0, const float* bias_s,
+                                             const float* rrow, uint8_t* stg, int r) {
+  tc_stage_chunk<ACT, RM, 0>(a, tot, h, nchunk, n0, bias_s, rrow, stg, r);
+  tc_stage_chunk<ACT, RM, 1>(a, tot, h, nchunk, n0, bias_s, rrow, stg, r);
+  tc_stage_chunk<ACT, RM, 2>(a, tot, h, nchunk, n0, bias_s, rrow, stg, r);
+}
+
 // One instantiation per activation and residual mode (RM 0 none, 1 added
 // before the activation, 2 after): each carries a single epilogue, which keeps
 // the code that the producer, TMA and MMA warps run beside it small.
@@ -652,11 +735,12 @@ template <int ACT, int RM>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap_hi,
                    const __grid_constant__ CUtensorMap wmap_lo,
-                   const __grid_constant__ CUtensorMap amap, const TcArgs a) {
+                   const __grid_constant__ CUtensorMap amap,
+                   const __grid_constant__ CUtensorMap ymap, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int S = a.stages;
-  const TcSmem L = TcSmem::make(a.bn, S, a.kout);
+  const TcSmem L = TcSmem::make(a.bn, S, a.kout, a.stg_chunks);
   float* bias_s = (float*)(smem + L.bias);
   const uint32_t b_bytes = (uint32_t)a.bn * 128;
   uint64_t* bars = (uint64_t*)(smem + L.bars);
@@ -945,6 +1029,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int tstep = grp ? 2 : 1;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const int nchunk = a.bn >> 4;
+    uint8_t* stg = smem + L.stg + (size_t)(warp - TC_WARP_EPI) * a.stg_chunks * TC_STG_BOX;
     int64_t tc = grp ? eg : 0;
     bool alive = true;
     for (int64_t tile = blockIdx.x + tc * gridDim.x; tile < a.tiles && alive;
@@ -1003,13 +1088,57 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const TcTile t = tc_tile(a, (int)(tile / a.n_tiles));
       const int n0 = (int)(tile % a.n_tiles) * a.bn;
       int n_ = 0, oh_ = 0, ow_ = 0;
-      if (!tc_row(a, t, q * 32 + lane, n_, oh_, ow_)) continue;
+      const bool valid = tc_row(a, t, q * 32 + lane, n_, oh_, ow_);
+      if (a.stg_chunks > 0) {
+        // Staged: the warp writes its 32 rows into its boxes, then lane 0
+        // stores each box with TMA (rows and channels outside the output are
+        // clipped by the tensor map).  Before the boxes are rewritten, the
+        // warp's previous stores must have read them.
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+        const float* rrow =
+            RM != 0 && valid ? a.res + ((int64_t)n_ * a.rs0 + (int64_t)oh_ * a.rs2 + (int64_t)ow_ * a.rs3)
+                             : nullptr;
+        tc_stage_row<ACT, RM>(a, tot, h, nchunk, n0, bias_s, rrow, stg, lane);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          int sx = 0, sy = 0;  // first pixel of the warp's 32 rows
+          bool inside;
+          if (a.amode == TC_A_RECT) {
+            const int r0 = q * 32;
+            sy = t.oh0 + r0 / a.tw;
+            sx = t.ow0 + (a.tw >= 32 ? r0 % a.tw : 0);
+            inside = sx < a.ow && sy < a.oh;
+          } else {
+            sy = t.m0 + q * 32;
+            inside = sy < a.m_total;
+          }
+          if (inside) {
+#pragma unroll
+            for (int j = 0; j < TC_EPI_CHUNKS; ++j) {
+              const int c = grp ? j : h + 2 * j;
+              if (c < nchunk && n0 + 16 * c < a.kout) {
+                if (a.amode == TC_A_RECT)
+                  tma_store_4d(&ymap, stg + j * TC_STG_BOX, n0 + 16 * c, sx, sy, t.n);
+                else
+                  tma_store_2d(&ymap, stg + j * TC_STG_BOX, n0 + 16 * c, sy);
+              }
+            }
+          }
+          bulk_commit();
+        }
+        continue;
+      }
+      if (!valid) continue;
       float* yrow = a.y + ((int64_t)n_ * a.ys0 + (int64_t)oh_ * a.ys2 + (int64_t)ow_ * a.ys3);
       const float* rrow =
           RM != 0 ? a.res + ((int64_t)n_ * a.rs0 + (int64_t)oh_ * a.rs2 + (int64_t)ow_ * a.rs3)
                   : nullptr;
       tc_finish_row<ACT, RM>(a, tot, h, nchunk, n0, bias_s, yrow, rrow);
     }
+    // No store may still read the staging boxes when the CTA exits.
+    if (a.stg_chunks > 0 && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -1052,7 +1181,8 @@ std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 // `estr` (traversal strides, default 1): a box dimension of b elements with
 // traversal stride t brings ceil(b / t) elements, stored densely.
 int encode_tiled(const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
-                 const cuuint32_t* box, CUtensorMap* out, const cuuint32_t* estr = nullptr) {
+                 const cuuint32_t* box, CUtensorMap* out, const cuuint32_t* estr = nullptr,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -1068,7 +1198,7 @@ int encode_tiled(const void* base, int rank, const cuuint64_t* dims, const cuuin
   }
   const cuuint32_t ones[5] = {1, 1, 1, 1, 1};
   CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, (void*)base, dims,
-                      strides, box, estr ? estr : ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      strides, box, estr ? estr : ones, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(MM_ERR_CUDA, "mm_conv2d_tc: cuTensorMapEncodeTiled failed (CUresult " +
@@ -1106,7 +1236,8 @@ bool aligned16(const void* p) { return (((uintptr_t)p) & 15) == 0; }
 
 // Dynamic shared memory one CTA may request on the current device: the
 // opt-in maximum minus the kernel's static shared memory.
-using TcKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const TcArgs);
+using TcKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                          const TcArgs);
 constexpr int TC_VARIANTS = 12;  // 4 activations x 3 residual modes
 
 template <int ACT>
@@ -1294,12 +1425,41 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   MM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   size_t smem_limit = 0;
   if ((rc = tc_smem_limit(dev, &smem_limit)) != MM_OK) return rc;
+  // Output tensor map for the staged TMA-store epilogue: a 4-D {K, W, H, N}
+  // map (box: 16 channels x one warp's 32 pixels of a rectangle) for
+  // rectangle tiles, a 2-D {K, pixels} map (box 16 x 32) for flat tiles when
+  // the output pixels are uniformly strided.  Otherwise rows are stored
+  // directly.
+  const int nchunk = a.bn / 16;
+  CUtensorMap ymap;
+  memset(&ymap, 0, sizeof(ymap));
+  bool staged = false;
+  if (nhwc_ok(y)) {
+    if (a.amode == TC_A_RECT) {
+      const cuuint64_t dims[4] = {(cuuint64_t)k_out, (cuuint64_t)ow, (cuuint64_t)oh, (cuuint64_t)n};
+      const cuuint64_t strides[3] = {(cuuint64_t)y->stride[3] * 4, (cuuint64_t)y->stride[2] * 4,
+                                     (cuuint64_t)y->stride[0] * 4};
+      const cuuint32_t box[4] = {16, (cuuint32_t)(a.tw >= 32 ? 32 : a.tw),
+                                 (cuuint32_t)(a.tw >= 32 ? 1 : 32 / a.tw), 1};
+      staged = encode_tiled(y->data, 4, dims, strides, box, &ymap, nullptr,
+                            CU_TENSOR_MAP_SWIZZLE_64B) == MM_OK;
+    } else if (y->stride[2] == ow * y->stride[3] && y->stride[0] == oh * y->stride[2]) {
+      const cuuint64_t dims[2] = {(cuuint64_t)k_out, (cuuint64_t)m_total};
+      const cuuint64_t strides[1] = {(cuuint64_t)y->stride[3] * 4};
+      const cuuint32_t box[2] = {16, 32};
+      staged = encode_tiled(y->data, 2, dims, strides, box, &ymap, nullptr,
+                            CU_TENSOR_MAP_SWIZZLE_64B) == MM_OK;
+    }
+  }
+  // Staging per epilogue warp: its chunks of one tile (all of them when the
+  // two-group epilogue may be chosen, bn <= 48; half of them otherwise).
+  const int stg_bound = staged ? (a.bn <= 16 * TC_EPI_CHUNKS ? nchunk : (nchunk + 1) / 2) : 0;
   // Two cross-term sets when at least 4 stages still fit, else one.
   int stages = 0;
   for (int xbuf = 2; xbuf >= 1 && stages == 0; --xbuf) {
     for (int st = TC_MAX_STAGES; st >= (xbuf == 2 ? 4 : 3); --st) {
       if (TC_LO_COLS * st + (4 + xbuf) * a.bn <= (int)TC_TMEM_COLS &&
-          TcSmem::make(a.bn, st, k_out).bytes() <= smem_limit) {
+          TcSmem::make(a.bn, st, k_out, stg_bound).bytes() <= smem_limit) {
         stages = st;
         a.xbuf = xbuf;
         break;
@@ -1309,8 +1469,9 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   if (stages == 0) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: N tile too wide");
   a.stages = stages;
   a.epi_groups = (a.period >= a.kb_total && a.xbuf == 2 && a.bn <= 16 * TC_EPI_CHUNKS) ? 2 : 1;
+  a.stg_chunks = staged ? (a.epi_groups == 2 ? nchunk : (nchunk + 1) / 2) : 0;
   const int64_t ktot = (int64_t)r * s * c_pad;
-  size_t smem = TcSmem::make(a.bn, stages, k_out).bytes();
+  size_t smem = TcSmem::make(a.bn, stages, k_out, a.stg_chunks).bytes();
 
   CUtensorMap mhi, mlo;
   if ((rc = weight_map(w_hi, ktot, k_pad, a.bn, &mhi)) != MM_OK) return rc;
@@ -1347,7 +1508,7 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   }
   // Persistent CTAs: one per SM.
   const int64_t ctas = a.tiles < (int64_t)sm_count() ? a.tiles : (int64_t)sm_count();
-  kernel<<<(unsigned)ctas, TC_THREADS, smem, resolve_stream(stream)>>>(mhi, mlo, amap, a);
+  kernel<<<(unsigned)ctas, TC_THREADS, smem, resolve_stream(stream)>>>(mhi, mlo, amap, ymap, a);
   MM_LAUNCH_CHECK("mm_conv2d_tc launch");
   return MM_OK;
 }
