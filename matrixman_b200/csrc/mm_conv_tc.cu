@@ -1434,7 +1434,8 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   CUtensorMap ymap;
   memset(&ymap, 0, sizeof(ymap));
   bool staged = false;
-  if (nhwc_ok(y)) {
+  // (A 16-channel tile gains nothing from staging: one box per warp.)
+  if (nhwc_ok(y) && a.bn >= 32) {
     if (a.amode == TC_A_RECT) {
       const cuuint64_t dims[4] = {(cuuint64_t)k_out, (cuuint64_t)ow, (cuuint64_t)oh, (cuuint64_t)n};
       const cuuint64_t strides[3] = {(cuuint64_t)y->stride[3] * 4, (cuuint64_t)y->stride[2] * 4,
