@@ -1354,9 +1354,15 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
     a.bn = ((per + 15) / 16) * 16;
   }
   a.n_tiles = (k_out + a.bn - 1) / a.bn;
-  // Promotion period: 4 k-blocks; reductions of up to 12 k-blocks (48 hi*hi
-  // MMAs per accumulator, drift < 2e-6 relative) take one period per tile.
-  a.period = a.kb_total <= 12 ? a.kb_total : 4;
+  // Promotion period: at most 12 k-blocks (48 MMAs per accumulator), balanced
+  // over the tile (18 -> 2 x 9, 36 -> 3 x 12).  The tensor core's truncating
+  // accumulation biases one period's sum by up to ~2.5e-6 relative
+  // (all-positive data); promotion into the fp32 total keeps that bias from
+  // growing with the reduction length.
+  {
+    const int np = (a.kb_total + 11) / 12;
+    a.period = (a.kb_total + np - 1) / np;
+  }
   a.act = p->act;
   a.res_before_act = p->residual_before_act;
   a.vec_store = nhwc_ok(y) ? 1 : 0;

@@ -115,24 +115,29 @@ def test_tc_matches_simt_path(mm):
     assert max_rel_err(y_tc, y_simt) < 1e-5
 
 
-def test_tc_deep_reduction_unbiased(mm):
+def test_tc_deep_reduction_drift_bounded(mm):
     """All-positive data is the worst case for the tensor core's truncating
-    accumulation (every partial sum moves away from zero).  With period
-    promotion the error stays at fp32 rounding level over 144 k-blocks."""
-    g = gen(21)
-    c, k = 512, 64
-    conv = nn.Conv2d(c, k, 3, 1, 1, bias=False)
-    with torch.no_grad():
-        conv.weight.copy_(torch.rand(conv.weight.shape, generator=g) / (c * 9))
-    unit = PreparedConv2d(conv, 0)
-    x = torch.rand(1, c, 12, 12, generator=g)
-    ref = O.conv2d(x, conv.weight.detach(), None, 1, 1)
-    y = unit(nhwc(mm, x)).cpu()
-    err = max_rel_err(y, ref)
-    assert err < 5e-6, f"max relative error {err:.3g}"
-    # no systematic drift: mean signed relative deviation near zero
-    drift = ((y - ref) / ref.abs().clamp_min(1e-30)).mean().item()
-    assert abs(drift) < 1e-6, f"mean drift {drift:.3g}"
+    accumulation (every partial sum moves toward zero).  Each period (at most 12
+    k-blocks) is promoted into an fp32 total with round-to-nearest adds, so the
+    bias is that of one period and must not grow with the reduction length:
+    144 k-blocks against 36 on the same data distribution."""
+    drifts = {}
+    for c, seed in ((512, 21), (128, 24)):
+        g = gen(seed)
+        k = 64
+        conv = nn.Conv2d(c, k, 3, 1, 1, bias=False)
+        with torch.no_grad():
+            conv.weight.copy_(torch.rand(conv.weight.shape, generator=g) / (c * 9))
+        unit = PreparedConv2d(conv, 0)
+        x = torch.rand(1, c, 12, 12, generator=g)
+        ref = O.conv2d(x, conv.weight.detach(), None, 1, 1)
+        y = unit(nhwc(mm, x)).cpu()
+        err = max_rel_err(y, ref)
+        assert err < 5e-6, f"C={c}: max relative error {err:.3g}"
+        # mean signed relative deviation: the truncation bias of one period
+        drifts[c] = ((y - ref) / ref.abs().clamp_min(1e-30)).mean().item()
+        assert abs(drifts[c]) < 3e-6, f"C={c}: mean drift {drifts[c]:.3g}"
+    assert abs(drifts[512]) < 1.25 * abs(drifts[128]) + 2e-7, f"drift grows with K: {drifts}"
 
 
 @pytest.mark.parametrize("m,k,n,act", [
