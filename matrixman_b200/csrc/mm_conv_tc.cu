@@ -1368,7 +1368,9 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   a.vec_store = nhwc_ok(y) ? 1 : 0;
   a.res_vec = residual && nhwc_ok(residual) ? 1 : 0;
   // How A tiles arrive (see TC_A_*).  Rectangles are chosen when they cover
-  // the output with little overhang.
+  // at least 60 % of their area with output pixels: TMA loads beat the gather
+  // mode by enough that a 20-pixel-wide output (best cover 62.5 %) runs about
+  // 30 % faster as rectangles despite the idle rows.
   a.amode = TC_A_GATHER;
   a.tw = a.th = a.ntw = a.nth = 1;
   {
@@ -1394,7 +1396,7 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
           a.nth = (int)nth;
         }
       }
-      if (best >= 0.8 && (int64_t)n * a.ntw * a.nth <= 0x7fffffffLL) a.amode = TC_A_RECT;
+      if (best >= 0.6 && (int64_t)n * a.ntw * a.nth <= 0x7fffffffLL) a.amode = TC_A_RECT;
     }
   }
   // A tensor map for the TMA modes (a map the driver rejects falls back to

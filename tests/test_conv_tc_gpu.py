@@ -63,6 +63,7 @@ def run_case(mm, n, c, k, ksz, stride, pad, hw, act=2, residual=None, seed=0):
     (1, 128, 144, 1, 1, 0, 12),   # K not a multiple of 16 tile
     (1, 96, 576, 3, 2, 1, 10),    # K > 256: three N tiles
     (3, 256, 256, 3, 1, 1, 7),    # deep layer
+    (2, 128, 128, 3, 1, 1, 20),   # 20 x 23 output: rectangles covering ~62 % (idle rows clipped)
     (1, 64, 64, 7, 2, 3, 23),     # 7x7 stride 2
 ])
 def test_tc_conv_geometries(mm, n, c, k, ksz, stride, pad, hw):
