@@ -46,7 +46,7 @@ def parse_args():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--batch", type=int, default=BATCH)
     p.add_argument("--e2e-steps", type=int, default=None)
-    p.add_argument("--e2e-chunks", type=int, default=3,
+    p.add_argument("--e2e-chunks", type=int, default=4,
                    help="1 GPU: matrixman.infer chunks (upload / forward / readback overlap)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile-case", action="store_true",

@@ -92,3 +92,18 @@ def test_infer_pipeline_matches_serial(mm, chunks):
     assert y.shape == ref.shape
     assert max_rel_err(y, ref) < 1e-6
     assert torch.equal(y, y2)
+
+
+def test_infer_explicit_sizes(mm):
+    """Uneven explicit slices give the serial values; bad sizes are rejected."""
+    import workloads as W
+    prepared = mm.prepare(W.yolov8_model("n"))
+    x = mm.pinned_empty((7, 3, 256, 256))
+    x.copy_(W.yolo_input(7, size=256))
+    with torch.no_grad():
+        ref = prepared(mm.to_device(x)).cpu()
+        y = mm.infer(prepared, x, sizes=[1, 2, 3, 1])
+        assert max_rel_err(y, ref) < 1e-6
+        for bad in ([3, 3], [7, 0], [8, -1], []):
+            with pytest.raises(ValueError):
+                mm.infer(prepared, x, sizes=bad)

@@ -24,6 +24,19 @@ def test_batch_slices_cover_batch_in_order():
             assert sizes == sorted(sizes, reverse=True)
 
 
+def test_infer_ramp_slices_cover_batch():
+    from matrixman_b200.pipeline import ramp_slices
+    assert [e - s for s, e in ramp_slices(64, 4)] == [8, 16, 24, 16]
+    assert ramp_slices(0, 4) == []
+    for batch in (1, 2, 3, 7, 22, 64, 65, 257):
+        for chunks in (1, 2, 3, 4, 5, 8):
+            sl = ramp_slices(batch, chunks)
+            assert len(sl) == min(chunks, batch)
+            assert sl[0][0] == 0 and sl[-1][1] == batch
+            assert all(a[1] == b[0] for a, b in zip(sl, sl[1:]))
+            assert all(e > s for s, e in sl)
+
+
 def test_batch_slices_rejects_bad_arguments():
     with pytest.raises(ValueError):
         batch_slices(4, 0)
