@@ -187,6 +187,9 @@ def run_b200(args):
         # PrivateUse1 device, so torch's accelerator check sees CUDA.
         from datetime import timedelta
         torch.cuda.set_device(local)
+        # NCCL's version banner goes to stdout; keep rank 0's stdout to the one
+        # JSON line unless the caller asked for NCCL logging.
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
 
