@@ -157,13 +157,30 @@ __global__ void copy_strided_kernel(const T* __restrict__ x, T* __restrict__ y, 
 // 16-byte aligned rows (NHWC channel slices: cat / split materialisation).
 // One warp per row (grid-stride over rows), lanes stride over the row's
 // float4s: coalesced 16-byte accesses, no per-element index division.
+// Row copy (concatenation into NHWC channel slices): rows x cols4 float4
+// elements over a flat index, so short rows leave no lane idle; each thread
+// has four independent loads in flight before its stores.
 __global__ void copy_rows_vec4_kernel(const float* __restrict__ x, float* __restrict__ y,
                                       int64_t rows, int cols4, int64_t xs, int64_t ys) {
-  const int64_t wstride = (int64_t)gridDim.x * blockDim.y;
-  for (int64_t r = blockIdx.x * (int64_t)blockDim.y + threadIdx.y; r < rows; r += wstride) {
-    const float4* src = reinterpret_cast<const float4*>(x + r * xs);
-    float4* dst = reinterpret_cast<float4*>(y + r * ys);
-    for (int c = threadIdx.x; c < cols4; c += 32) dst[c] = __ldg(src + c);
+  const int64_t total = rows * cols4;
+  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e0 < total; e0 += 4 * nth) {
+    float4 v[4];
+    int64_t dofs[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t e = e0 + u * nth;
+      dofs[u] = -1;
+      if (e < total) {
+        const int64_t r = e / cols4;
+        const int64_t c = e - r * cols4;
+        v[u] = __ldg(reinterpret_cast<const float4*>(x + r * xs) + c);
+        dofs[u] = r * ys + 4 * c;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (dofs[u] >= 0) *reinterpret_cast<float4*>(y + dofs[u]) = v[u];
   }
 }
 
@@ -457,6 +474,28 @@ __global__ void upsample_nearest_nhwc4_kernel(const float* __restrict__ x, float
     int64_t ix = nearest_src(ox, p.w, p.ow, scale_w);
     float4 v = *reinterpret_cast<const float4*>(x + n * p.xs[0] + c + iy * p.xs[2] + ix * p.xs[3]);
     *reinterpret_cast<float4*>(y + n * p.ys[0] + c + oy * p.ys[2] + ox * p.ys[3]) = v;
+  }
+}
+
+// Exact 2x nearest upsample of NHWC float4 rows (output = 2 x input in both
+// dimensions, where the source index is dst >> 1): each thread reads one input
+// float4 and writes the 2 x 2 output block; blockIdx.y walks input rows.
+__global__ void upsample2x_nhwc4_kernel(const float* __restrict__ x, float* __restrict__ y, Pool4 p) {
+  const int c4 = (int)(p.c >> 2);
+  const int row_elems = (int)p.w * c4;
+  for (int64_t row = blockIdx.y; row < p.n * p.h; row += gridDim.y) {
+    const int64_t n = row / p.h, iy = row - n * p.h;
+    const float* xr = x + n * p.xs[0] + iy * p.xs[2];
+    float* yr = y + n * p.ys[0] + 2 * iy * p.ys[2];
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < row_elems; e += gridDim.x * blockDim.x) {
+      const int ix = e / c4, c = (e - ix * c4) * 4;
+      const float4 v = *reinterpret_cast<const float4*>(xr + ix * p.xs[3] + c);
+      float* o = yr + 2 * ix * p.ys[3] + c;
+      *reinterpret_cast<float4*>(o) = v;
+      *reinterpret_cast<float4*>(o + p.ys[3]) = v;
+      *reinterpret_cast<float4*>(o + p.ys[2]) = v;
+      *reinterpret_cast<float4*>(o + p.ys[2] + p.ys[3]) = v;
+    }
   }
 }
 
@@ -807,10 +846,12 @@ static int copy_impl(const mm_tensor_t* x_in, const mm_tensor_t* y_in, cudaStrea
     const int64_t rows = g[0].size[0];
     const int64_t cols4 = g[0].size[1] / 4;
     if (cols4 > 0x7fffffff) return fail(MM_ERR_UNSUPPORTED, "mm_copy: row too long");
-    int64_t blocks = (rows + 7) / 8;
+    const int64_t elems = rows * cols4;
+    int64_t blocks = (elems + 4 * 256 - 1) / (4 * 256);
     const int64_t cap = (int64_t)sm_count() * 16;
     if (blocks > cap) blocks = cap;
-    copy_rows_vec4_kernel<<<(unsigned)blocks, dim3(32, 8), 0, s>>>(
+    if (blocks < 1) blocks = 1;
+    copy_rows_vec4_kernel<<<(unsigned)blocks, 256, 0, s>>>(
         (const float*)x->data, (float*)y->data, rows, (int)cols4, g[0].stride[0], g[1].stride[0]);
     MM_LAUNCH_CHECK("mm_copy launch");
     return MM_OK;
@@ -1051,7 +1092,12 @@ extern "C" int mm_upsample_nearest2d(const mm_tensor_t* x, double scale_h, doubl
                p.xs[2] % 4 == 0 && p.xs[3] % 4 == 0 && p.ys[2] % 4 == 0 && p.ys[3] % 4 == 0 &&
                p.xs[0] % 4 == 0 && p.ys[0] % 4 == 0 &&
                ((((uintptr_t)x->data) | ((uintptr_t)y->data)) & 15) == 0;
-  if (nhwc4) {
+  if (nhwc4 && p.oh == 2 * p.h && p.ow == 2 * p.w && p.w * (p.c / 4) <= 0x7fffffffLL) {
+    const int64_t row_elems = p.w * (p.c / 4);
+    const dim3 grid((unsigned)std::min<int64_t>((row_elems + 255) / 256, 1024),
+                    (unsigned)std::min<int64_t>(p.n * p.h, 65535));
+    upsample2x_nhwc4_kernel<<<grid, 256, 0, s>>>((const float*)x->data, (float*)y->data, p);
+  } else if (nhwc4) {
     upsample_nearest_nhwc4_kernel<<<grid_for(total / 4, 256, (int64_t)sm_count() * 8), 256, 0, s>>>(
         (const float*)x->data, (float*)y->data, p, fh, fw);
   } else {
