@@ -404,6 +404,60 @@ __global__ void sppf_kernel(const float* __restrict__ x, float* __restrict__ y1,
   }
 }
 
+// SPPF on whole small images: one block per (image, group of SPPF_CG
+// channels) holds the image in shared memory and runs SPPF's definition --
+// three chained 5x5 stride-1 max-pools with -inf padding -- as row and column
+// passes between two buffers, writing each pool's result to its slice.  The
+// input is read once (the tiled kernel re-reads 6.25x for its halos at 20 x 20).
+__global__ void sppf_image_kernel(const float* __restrict__ x, float* __restrict__ y1,
+                                  float* __restrict__ y2, float* __restrict__ y3, Pool4 p, Pool4 q2,
+                                  Pool4 q3, int cgroups) {
+  extern __shared__ float sp_buf[];
+  const int H = (int)p.h, W = (int)p.w, HW = H * W;
+  float* a = sp_buf;                    // [H][W][SPPF_CG]
+  float* b = sp_buf + HW * SPPF_CG;
+  const int n = blockIdx.x / cgroups;
+  const int c0 = (blockIdx.x - n * cgroups) * SPPF_CG;
+  const int total = HW * SPPF_CG;
+  for (int e = threadIdx.x; e < total; e += blockDim.x) {
+    const int cc = e % SPPF_CG, pix = e / SPPF_CG;
+    const int yy = pix / W, xx = pix - yy * W;
+    const int c = c0 + cc;
+    a[e] = c < p.c ? x[n * p.xs[0] + c * p.xs[1] + yy * p.xs[2] + xx * p.xs[3]] : 0.f;
+  }
+  __syncthreads();
+  for (int round = 0; round < 3; ++round) {
+    for (int e = threadIdx.x; e < total; e += blockDim.x) {  // rows: a -> b
+      const int cc = e % SPPF_CG, pix = e / SPPF_CG;
+      const int yy = pix / W, xx = pix - yy * W;
+      float m = -INFINITY;
+#pragma unroll
+      for (int d = -2; d <= 2; ++d) {
+        const int xs = xx + d;
+        if (xs >= 0 && xs < W) m = nanmax(m, a[(yy * W + xs) * SPPF_CG + cc]);
+      }
+      b[e] = m;
+    }
+    __syncthreads();
+    float* yo = round == 0 ? y1 : round == 1 ? y2 : y3;
+    const Pool4& q = round == 0 ? p : round == 1 ? q2 : q3;
+    for (int e = threadIdx.x; e < total; e += blockDim.x) {  // columns: b -> a, store
+      const int cc = e % SPPF_CG, pix = e / SPPF_CG;
+      const int yy = pix / W, xx = pix - yy * W;
+      float m = -INFINITY;
+#pragma unroll
+      for (int d = -2; d <= 2; ++d) {
+        const int ys = yy + d;
+        if (ys >= 0 && ys < H) m = nanmax(m, b[(ys * W + xx) * SPPF_CG + cc]);
+      }
+      a[e] = m;
+      const int c = c0 + cc;
+      if (c < p.c) yo[n * q.ys[0] + c * q.ys[1] + yy * q.ys[2] + xx * q.ys[3]] = m;
+    }
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Reduction (sum/mean) over a dim mask: one warp per output element.
 // ---------------------------------------------------------------------------
@@ -988,8 +1042,21 @@ extern "C" int mm_sppf_pool(const mm_tensor_t* x, const mm_tensor_t* y1, const m
   if (rc != MM_OK) return rc;
   if (p.oh != p.h || p.ow != p.w || q2.oh != p.h || q2.ow != p.w || q3.oh != p.h || q3.ow != p.w)
     return fail(MM_ERR_INVALID, "mm_sppf_pool: outputs must match the input's spatial size");
-  int64_t tiles_w = (p.w + SPPF_TW - 1) / SPPF_TW, tiles_h = (p.h + SPPF_TH - 1) / SPPF_TH;
   int64_t cgroups = (p.c + SPPF_CG - 1) / SPPF_CG;
+  {
+    // Whole image per block when two copies of it fit in 48 KB of shared memory.
+    const int64_t bytes = 2 * p.h * p.w * SPPF_CG * (int64_t)sizeof(float);
+    const int64_t blocks = p.n * cgroups;
+    if (bytes <= 48 * 1024 && blocks > 0 && blocks <= 0x7fffffffLL) {
+      cudaStream_t s = resolve_stream(stream);
+      sppf_image_kernel<<<(unsigned)blocks, 256, (size_t)bytes, s>>>(
+          (const float*)x->data, (float*)y1->data, (float*)y2->data, (float*)y3->data, p, q2, q3,
+          (int)cgroups);
+      MM_LAUNCH_CHECK("mm_sppf_pool launch");
+      return MM_OK;
+    }
+  }
+  int64_t tiles_w = (p.w + SPPF_TW - 1) / SPPF_TW, tiles_h = (p.h + SPPF_TH - 1) / SPPF_TH;
   int64_t blocks = p.n * cgroups * tiles_h * tiles_w;
   if (blocks == 0) return MM_OK;
   if (blocks > 0x7fffffffLL) return fail(MM_ERR_UNSUPPORTED, "mm_sppf_pool: tensor too large");

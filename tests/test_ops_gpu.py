@@ -245,6 +245,14 @@ def test_sppf_fused_chain_bit_exact(mm):
                 d.runtime.stream)
     for o, r in zip(outs, O.sppf_chain(x)):
         assert bit_exact(o.cpu(), r)
+    # a partial channel group and a tiny image
+    x = torch.randn(1, 12, 7, 9, generator=gen(31))
+    d = nhwc(mm, x)
+    outs = [ops.empty(d.runtime, x.shape, d._logical_strides) for _ in range(3)]
+    ops._launch("mm_sppf_pool", ctypes.byref(d.desc()), *(ctypes.byref(o.desc()) for o in outs),
+                d.runtime.stream)
+    for o, r in zip(outs, O.sppf_chain(x)):
+        assert bit_exact(o.cpu(), r)
 
 
 @pytest.mark.parametrize("k,s,p,ceil,cip,div", [(2, 2, 0, False, True, None), (3, 2, 1, True, False, None),
