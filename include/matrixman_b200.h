@@ -374,6 +374,31 @@ int mm_gemm(const mm_tensor_t* x, const mm_tensor_t* w, const mm_tensor_t* bias,
 int mm_yolo_decode(const mm_tensor_t* const* feats, const float* strides, int nlevels, int reg_max,
                    int nc, const mm_tensor_t* out, void* stream);
 
+/* Detection reduction: pred [B, 4+classes, anchors] -> out [B, 6, anchors] =
+ * (cx, cy, w, h, best score, best class index as float); the best score starts
+ * at -1 and a class replaces it only when strictly greater.  Replaces
+ * reduce_detection_output (backends/opengl/ops/postprocessing.py:87-119, the
+ * shader at :35-52), exposed as gpu_postprocess_detection (backend.py:263-266);
+ * the reference accepts B = 1 only. */
+int mm_detect_reduce(const mm_tensor_t* pred, const mm_tensor_t* out, void* stream);
+
+/* Largest number of candidates (anchors at or above the confidence threshold)
+ * one image may have in mm_detect_nms. */
+#define MM_DETECT_MAX_CANDIDATES 4096
+
+/* Confidence filter, box conversion and per-class greedy NMS on the device, per
+ * image: the reference's CPU detections() (demo/yolo_helpers.py:91-137, NMS at
+ * :59-89).  Candidates: best class (first maximum) with score >= conf_thr;
+ * boxes (cx - w/2, cy - h/2, cx + w/2, cy + h/2) clamped to [0, width-1] x
+ * [0, height-1]; NMS keeps a candidate only if IoU <= iou_thr against every
+ * earlier kept candidate of its class, in descending score order (equal scores
+ * by anchor index).  dets [B, max_det, 6] receives the first max_det kept
+ * (x1, y1, x2, y2, score, class) in descending score order and counts (device
+ * int32[B]) their number; an image with more than MM_DETECT_MAX_CANDIDATES
+ * candidates is skipped with counts[b] = -(candidates). */
+int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_thr, float width, float height,
+                  int max_det, const mm_tensor_t* dets, int32_t* counts, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

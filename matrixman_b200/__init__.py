@@ -33,6 +33,7 @@ from .api import (
     unsupported_report,
 )
 from .pipeline import infer
+from .detect import postprocess_detections
 from .preparation import auto_prepare, prepare, prepare_cuda, prepare_opengl
 from .tensor import Gm45Tensor, MatrixManTensor, install_tensor_method, is_matrixman_tensor
 
@@ -98,6 +99,7 @@ sys.modules[__name__].__class__ = _MatrixManModule
 
 __all__ = [
     "infer",
+    "postprocess_detections",
     "MatrixManTensor", "Gm45Tensor", "auto_prepare", "config", "debug_enabled", "device_count",
     "gpu_postprocess_detection", "init", "install_tensor_method", "is_gm45_tensor",
     "is_matrixman_tensor", "prefer", "prepare", "prepare_cuda", "prepare_opengl", "profile",

@@ -176,6 +176,8 @@ SIGNATURES = {
     "mm_kernel_error": [_i, ctypes.POINTER(_i), _i],
     "mm_gemm": [_T, _T, _T, _d, _d, _i, _T, _vp],
     "mm_yolo_decode": [_TT, ctypes.POINTER(ctypes.c_float), _i, _i, _i, _T, _vp],
+    "mm_detect_reduce": [_T, _T, _vp],
+    "mm_detect_nms": [_T, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _i, _T, _vp, _vp],
 }
 
 

@@ -175,4 +175,8 @@ def raw_texture(data):
 
 
 def gpu_postprocess_detection(value):
-    raise NotImplementedError("MatrixMan/CUDA: GPU detection postprocessing not implemented")
+    """[B, 4+classes, anchors] -> [B, 6, anchors] on the device (box, best
+    score, best class); see ``matrixman_b200.detect``."""
+    from .detect import reduce_detection_output
+
+    return reduce_detection_output(value)

@@ -156,3 +156,70 @@ def yolo_decode(feats, strides, reg_max=16, nc=80):
     dfl = DFL(reg_max)
     dbox = dist2bbox(dfl(box), anchors.transpose(0, 1).unsqueeze(0), dim=1) * stride_t.transpose(0, 1)
     return torch.cat((dbox, cls.sigmoid()), 1)
+
+
+def detect_reduce(pred: torch.Tensor) -> torch.Tensor:
+    """[B, 4+classes, anchors] -> [B, 6, anchors]: the box rows, the best class
+    score (starting at -1; a class replaces it only when strictly greater) and
+    its class index as float.  Restates the reference's detection-reduction
+    shader (drivers/matrixman/backends/opengl/ops/postprocessing.py:35-52),
+    batched."""
+    p = pred.to(torch.float32)
+    best = torch.full((p.shape[0], p.shape[2]), -1.0)
+    cls = torch.zeros((p.shape[0], p.shape[2]))
+    for c in range(p.shape[1] - 4):
+        s = p[:, 4 + c]
+        better = s > best
+        best = torch.where(better, s, best)
+        cls = torch.where(better, torch.full_like(cls, float(c)), cls)
+    return torch.cat((p[:, :4], best[:, None], cls[:, None]), 1)
+
+
+def _greedy_nms(boxes: torch.Tensor, scores: torch.Tensor, iou_threshold: float) -> list[int]:
+    """Greedy NMS with the reference's fallback arithmetic
+    (demo/yolo_helpers.py:70-89): keep the best remaining box, drop the rest
+    unless IoU <= threshold.  Equal scores keep their input order."""
+    keep = []
+    order = torch.sort(scores, descending=True, stable=True).indices
+    x1, y1, x2, y2 = boxes.unbind(1)
+    areas = (x2 - x1) * (y2 - y1)
+    while order.numel():
+        cur = order[0]
+        keep.append(int(cur))
+        if order.numel() == 1:
+            break
+        rest = order[1:]
+        xx1 = torch.maximum(x1[rest], x1[cur])
+        yy1 = torch.maximum(y1[rest], y1[cur])
+        xx2 = torch.minimum(x2[rest], x2[cur])
+        yy2 = torch.minimum(y2[rest], y2[cur])
+        inter = (xx2 - xx1).clamp_min(0) * (yy2 - yy1).clamp_min(0)
+        iou = inter / (areas[cur] + areas[rest] - inter).clamp_min(1e-12)
+        order = rest[iou <= iou_threshold]
+    return keep
+
+
+def detections(pred: torch.Tensor, width: int, height: int, conf_threshold: float,
+               iou_threshold: float) -> torch.Tensor:
+    """One image's [4+classes, anchors] prediction -> [n, 6] detections
+    (x1, y1, x2, y2, score, class) in descending score order: best class by
+    max/argmax (first maximum), score >= conf_threshold, corner boxes clamped to
+    [0, width-1] x [0, height-1], NMS per class.  Restates the reference's
+    detections() (demo/yolo_helpers.py:91-137)."""
+    p = pred.to(torch.float32).t()
+    boxes, scores = p[:, :4], p[:, 4:]
+    conf, cls = scores.max(dim=1).values, scores.argmax(dim=1)
+    keep = conf >= conf_threshold
+    if not keep.any():
+        return torch.zeros((0, 6))
+    boxes, conf, cls = boxes[keep], conf[keep], cls[keep]
+    cx, cy, w, h = boxes.unbind(1)
+    conv = torch.stack(((cx - w / 2).clamp(0, width - 1), (cy - h / 2).clamp(0, height - 1),
+                        (cx + w / 2).clamp(0, width - 1), (cy + h / 2).clamp(0, height - 1)), 1)
+    selected = []
+    for c in cls.unique(sorted=True).tolist():
+        idx = torch.nonzero(cls == c, as_tuple=False).flatten()
+        selected.extend(int(idx[k]) for k in _greedy_nms(conv[idx], conf[idx], iou_threshold))
+    sel = torch.tensor(selected, dtype=torch.long)
+    sel = sel[torch.sort(conf[sel], descending=True, stable=True).indices]
+    return torch.cat((conv[sel], conf[sel, None], cls[sel, None].to(torch.float32)), 1)

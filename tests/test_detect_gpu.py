@@ -1,0 +1,78 @@
+"""Detection postprocessing on the device against the CPU oracle (pinned to
+the reference's detections() by tests/golden/detect_vectors.npz)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops as O
+from oracle.tolerance import bit_exact
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden" / "detect_vectors.npz"
+
+
+def gen(seed):
+    g = torch.Generator()
+    g.manual_seed(seed)
+    return g
+
+
+def as_tensor(dets):
+    return torch.tensor([d[0] + [d[1], float(d[2])] for d in dets], dtype=torch.float32).reshape(-1, 6)
+
+
+def test_detect_reduce_matches_oracle(mm):
+    p = torch.rand(3, 24, 777, generator=gen(1)) * 4 - 2   # includes rows below -1
+    p[1, 4:, 5] = -3.0                                      # no class above -1: score -1, class 0
+    p[2, 7, 9] = p[2, 9, 9] = 5.0                           # tie: first maximum wins
+    y = mm.gpu_postprocess_detection(mm.to_device(p)).cpu()
+    assert bit_exact(y, O.detect_reduce(p))
+
+
+def test_nms_matches_reference_vectors(mm):
+    d = np.load(GOLDEN)
+    for name in ("small", "many_classes", "tight_iou"):
+        pred = torch.from_numpy(d[f"prediction_{name}"])
+        width, height, conf, iou = d[f"params_{name}"].tolist()
+        want = torch.from_numpy(d[f"detections_{name}"])
+        batch = torch.cat((pred, pred), 0)
+        got = mm.postprocess_detections(mm.to_device(batch), int(width), int(height), conf, iou,
+                                        max_det=4096)
+        assert len(got) == 2
+        for g in got:
+            assert bit_exact(as_tensor(g), want), name
+
+
+def test_nms_strided_view_and_max_det(mm):
+    d = np.load(GOLDEN)
+    pred = torch.from_numpy(d["prediction_small"])
+    width, height, conf, iou = d["params_small"].tolist()
+    want = torch.from_numpy(d["detections_small"])
+    # [B, anchors, 4+classes] on the device, viewed as [B, 4+classes, anchors]
+    view = mm.to_device(pred.transpose(1, 2).contiguous()).transpose(1, 2)
+    got = mm.postprocess_detections(view, int(width), int(height), conf, iou, max_det=10)
+    assert bit_exact(as_tensor(got[0]), want[:10])
+
+
+def test_nms_rejects_too_many_candidates(mm):
+    p = torch.rand(1, 6, 5000, generator=gen(2)) * 100
+    p[:, 4:] = 0.9
+    with pytest.raises(RuntimeError, match="candidates"):
+        mm.postprocess_detections(mm.to_device(p), 640, 640, 0.25, 0.45)
+
+
+def test_yolo_output_postprocessed_on_device(mm):
+    """The prepared YOLOv8n output at 256 x 256, post-processed on the device,
+    equals the oracle applied to the read-back output, image by image."""
+    import workloads as W
+    prepared = mm.prepare(W.yolov8_model("n"))
+    with torch.no_grad():
+        y = prepared(mm.to_device(W.yolo_input(3, size=256)))
+    got = mm.postprocess_detections(y, 256, 256, 0.3, 0.5, max_det=4096)
+    host = y.cpu()
+    assert len(got) == 3
+    for i in range(3):
+        want = O.detections(host[i], 256, 256, 0.3, 0.5)
+        assert bit_exact(as_tensor(got[i]), want)

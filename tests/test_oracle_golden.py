@@ -127,3 +127,28 @@ def test_metadata_helpers_match_reference():
     for c in cases["unsqueeze_shape_strides"]:
         s, st = T.unsqueeze_shape_strides(c["shape"], c["strides"], c["dim"])
         assert [list(s), list(st)] == c["result"]
+
+
+DETECT_CASES = ("small", "many_classes", "tight_iou")
+
+
+def test_detections_oracle_matches_reference_vectors():
+    """oracle.detections reproduces the reference's detections() output
+    (tests/golden/make_detect_golden.py) exactly: boxes, scores, classes, order."""
+    d = np.load(GOLDEN / "detect_vectors.npz")
+    for name in DETECT_CASES:
+        pred = torch.from_numpy(d[f"prediction_{name}"])
+        width, height, conf, iou = d[f"params_{name}"].tolist()
+        got = O.detections(pred[0], int(width), int(height), conf, iou)
+        want = torch.from_numpy(d[f"detections_{name}"])
+        assert got.shape == want.shape, name
+        assert bit_exact(got, want), name
+
+
+def test_detect_reduce_oracle_semantics():
+    """First maximum wins; the score starts at -1 (all-below -1 keeps class 0, score -1)."""
+    p = torch.tensor([[[1.0], [2.0], [3.0], [4.0], [0.5], [0.7], [0.7], [0.1]]])
+    r = O.detect_reduce(p)
+    assert r[0, :, 0].tolist() == [1.0, 2.0, 3.0, 4.0, 0.699999988079071, 1.0]
+    q = torch.tensor([[[0.0], [0.0], [1.0], [1.0], [-3.0], [-2.0]]])
+    assert O.detect_reduce(q)[0, 4:, 0].tolist() == [-1.0, 0.0]
