@@ -384,7 +384,7 @@ int mm_detect_reduce(const mm_tensor_t* pred, const mm_tensor_t* out, void* stre
 
 /* Largest number of candidates (anchors at or above the confidence threshold)
  * one image may have in mm_detect_nms. */
-#define MM_DETECT_MAX_CANDIDATES 4096
+#define MM_DETECT_MAX_CANDIDATES 12288
 
 /* Confidence filter, box conversion and per-class greedy NMS on the device, per
  * image: the reference's CPU detections() (demo/yolo_helpers.py:91-137, NMS at
@@ -398,6 +398,14 @@ int mm_detect_reduce(const mm_tensor_t* pred, const mm_tensor_t* out, void* stre
  * candidates is skipped with counts[b] = -(candidates). */
 int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_thr, float width, float height,
                   int max_det, const mm_tensor_t* dets, int32_t* counts, void* stream);
+
+/* Frame preprocessing: frames (device, contiguous uint8 [n, h, w, 3] BGR) ->
+ * out [n, 3, out_h, out_w] float32 RGB / 255, resized with OpenCV's 8-bit
+ * INTER_LINEAR fixed-point bilinear algorithm.  Replaces the reference's CPU
+ * preprocess_frame (demo/yolo_helpers.py:53-56: cv2.resize, cvtColor
+ * BGR2RGB, permute, / 255), so uploads carry uint8 frames. */
+int mm_preprocess_bgr8(const uint8_t* frames, int64_t n, int64_t h, int64_t w, const mm_tensor_t* out,
+                       void* stream);
 
 #ifdef __cplusplus
 }

@@ -34,6 +34,7 @@ from .api import (
 )
 from .pipeline import infer
 from .detect import postprocess_detections
+from .frames import preprocess_frames
 from .preparation import auto_prepare, prepare, prepare_cuda, prepare_opengl
 from .tensor import Gm45Tensor, MatrixManTensor, install_tensor_method, is_matrixman_tensor
 
@@ -100,6 +101,7 @@ sys.modules[__name__].__class__ = _MatrixManModule
 __all__ = [
     "infer",
     "postprocess_detections",
+    "preprocess_frames",
     "MatrixManTensor", "Gm45Tensor", "auto_prepare", "config", "debug_enabled", "device_count",
     "gpu_postprocess_detection", "init", "install_tensor_method", "is_gm45_tensor",
     "is_matrixman_tensor", "prefer", "prepare", "prepare_cuda", "prepare_opengl", "profile",

@@ -178,6 +178,7 @@ SIGNATURES = {
     "mm_yolo_decode": [_TT, ctypes.POINTER(ctypes.c_float), _i, _i, _i, _T, _vp],
     "mm_detect_reduce": [_T, _T, _vp],
     "mm_detect_nms": [_T, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _i, _T, _vp, _vp],
+    "mm_preprocess_bgr8": [_vp, _i64, _i64, _i64, _T, _vp],
 }
 
 

@@ -19,9 +19,10 @@
 //     The first max_det kept detections (x1, y1, x2, y2, score, class), in
 //     descending score order, go to dets[b]; counts[b] = their number.
 //
-// One CTA per image holds its candidates in shared memory (at most
-// MM_DETECT_MAX_CANDIDATES); an image with more candidates is not processed
-// and reports counts[b] = -(number of candidates).
+// One CTA per image holds its candidates' scores, classes and anchors in
+// shared memory (at most MM_DETECT_MAX_CANDIDATES); their boxes are recomputed
+// from the prediction (L2-resident) where needed.  An image with more
+// candidates is not processed and reports counts[b] = -(number of candidates).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -32,6 +33,8 @@
 namespace mm {
 
 constexpr int DET_CAP = MM_DETECT_MAX_CANDIDATES;
+constexpr int DET_SORT = 16384;  // power of two >= DET_CAP: the sort's length limit
+static_assert(DET_SORT >= DET_CAP && DET_CAP < 32768, "candidate indices are int16");
 constexpr int DET_THREADS = 1024;
 
 struct DetArgs {
@@ -71,17 +74,18 @@ __global__ void detect_reduce_kernel(const float* __restrict__ pred, int64_t ps0
   }
 }
 
-// Candidate arrays in dynamic shared memory (DET_CAP entries each).
+// Candidate arrays in dynamic shared memory.
 struct DetSmem {
-  float *x1, *y1, *x2, *y2, *score;
-  int *cls, *anchor;
-  int16_t* ord;   // sort order
-  int16_t* keep;  // kept candidates in order
-  uint8_t* sup;   // suppressed flags
+  float* score;    // [DET_CAP]
+  int* anchor;     // [DET_CAP]
+  int16_t* cls;    // [DET_CAP]
+  int16_t* keep;   // [DET_CAP] kept candidates in order
+  int16_t* ord;    // [DET_SORT] sort order
+  uint8_t* sup;    // [DET_CAP] suppressed flags
 };
 
 __host__ __device__ constexpr size_t det_smem_bytes() {
-  return (size_t)DET_CAP * (7 * 4 + 2 + 2 + 1) + 64;
+  return (size_t)DET_CAP * (4 + 4 + 2 + 2 + 1) + (size_t)DET_SORT * 2 + 64;
 }
 
 // torch.maximum / torch.minimum: NaN if either operand is NaN.
@@ -94,6 +98,16 @@ __device__ __forceinline__ float tmin(float a, float b) {
 
 __device__ __forceinline__ float clampf_keep_nan(float v, float hi) {
   return v < 0.f ? 0.f : (v > hi ? hi : v);
+}
+
+// Corner box of an anchor: (cx - w/2, cy - h/2, cx + w/2, cy + h/2) clamped
+// to [0, xmax] x [0, ymax], in the reference's operation order (w / 2 exact).
+__device__ __forceinline__ float4 det_box(const DetArgs& a, const float* pb, int anchor) {
+  const float* p = pb + (int64_t)anchor * a.ps2;
+  const float cx = p[0], cy = p[a.ps1], w = p[2 * a.ps1], h = p[3 * a.ps1];
+  const float hw = __fmul_rn(w, 0.5f), hh = __fmul_rn(h, 0.5f);
+  return make_float4(clampf_keep_nan(__fsub_rn(cx, hw), a.xmax), clampf_keep_nan(__fsub_rn(cy, hh), a.ymax),
+                     clampf_keep_nan(__fadd_rn(cx, hw), a.xmax), clampf_keep_nan(__fadd_rn(cy, hh), a.ymax));
 }
 
 // a before b in the NMS order: higher score first, then lower anchor index.
@@ -110,24 +124,17 @@ __device__ __forceinline__ bool det_after(const DetSmem& s, int x, int y) {
 
 __global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a) {
   extern __shared__ __align__(16) uint8_t det_raw[];
-  __shared__ int s_count, s_kept;
+  __shared__ int s_count;
   DetSmem s;
-  s.x1 = reinterpret_cast<float*>(det_raw);
-  s.y1 = s.x1 + DET_CAP;
-  s.x2 = s.y1 + DET_CAP;
-  s.y2 = s.x2 + DET_CAP;
-  s.score = s.y2 + DET_CAP;
-  s.cls = reinterpret_cast<int*>(s.score + DET_CAP);
-  s.anchor = s.cls + DET_CAP;
-  s.ord = reinterpret_cast<int16_t*>(s.anchor + DET_CAP);
-  s.keep = s.ord + DET_CAP;
-  s.sup = reinterpret_cast<uint8_t*>(s.keep + DET_CAP);
+  s.score = reinterpret_cast<float*>(det_raw);
+  s.anchor = reinterpret_cast<int*>(s.score + DET_CAP);
+  s.cls = reinterpret_cast<int16_t*>(s.anchor + DET_CAP);
+  s.keep = s.cls + DET_CAP;
+  s.ord = s.keep + DET_CAP;
+  s.sup = reinterpret_cast<uint8_t*>(s.ord + DET_SORT);
   const int64_t b = blockIdx.x;
   const int tid = threadIdx.x;
-  if (tid == 0) {
-    s_count = 0;
-    s_kept = 0;
-  }
+  if (tid == 0) s_count = 0;
   __syncthreads();
 
   // 1. Candidates: best class (first maximum), confidence filter, corner boxes.
@@ -146,14 +153,8 @@ __global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a) {
     if (best >= a.conf_thr) {
       const int slot = atomicAdd(&s_count, 1);
       if (slot < DET_CAP) {
-        const float cx = p[0], cy = p[a.ps1], w = p[2 * a.ps1], h = p[3 * a.ps1];
-        const float hw = __fmul_rn(w, 0.5f), hh = __fmul_rn(h, 0.5f);  // w / 2, exact
-        s.x1[slot] = clampf_keep_nan(__fsub_rn(cx, hw), a.xmax);
-        s.y1[slot] = clampf_keep_nan(__fsub_rn(cy, hh), a.ymax);
-        s.x2[slot] = clampf_keep_nan(__fadd_rn(cx, hw), a.xmax);
-        s.y2[slot] = clampf_keep_nan(__fadd_rn(cy, hh), a.ymax);
         s.score[slot] = best;
-        s.cls[slot] = bc;
+        s.cls[slot] = (int16_t)bc;
         s.anchor[slot] = (int)an;
       }
     }
@@ -191,28 +192,33 @@ __global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a) {
     }
   }
 
-  // 3. Greedy NMS in score order, suppressing within a class only.
-  int i = 0;
-  while (true) {
+  // 3. Greedy NMS in score order, suppressing within a class only.  Kept
+  // candidates are final once kept (only earlier kept ones suppress), so the
+  // pass ends after max_det of them.  nk is counted by every thread alike.
+  int i = 0, nk = 0;
+  while (nk < a.max_det) {
     // uniform: every thread reads the same flags (a padding slot, which the sort
     // never leaves among the first n, would count as suppressed)
     while (i < n && (s.ord[i] < 0 || s.sup[s.ord[i]])) ++i;
     if (i >= n) break;
     const int c = s.ord[i];
-    if (tid == 0) s.keep[s_kept++] = (int16_t)c;
-    const float cx1 = s.x1[c], cy1 = s.y1[c], cx2 = s.x2[c], cy2 = s.y2[c];
+    if (tid == 0) s.keep[nk] = (int16_t)c;
+    ++nk;
+    const float4 cb = det_box(a, pb, s.anchor[c]);
+    const float cx1 = cb.x, cy1 = cb.y, cx2 = cb.z, cy2 = cb.w;
     const float carea = __fmul_rn(__fsub_rn(cx2, cx1), __fsub_rn(cy2, cy1));
     const int ccls = s.cls[c];
     for (int j = i + 1 + tid; j < n; j += DET_THREADS) {
       const int r = s.ord[j];
       if (r < 0 || s.sup[r] || s.cls[r] != ccls) continue;
-      const float xx1 = tmax(s.x1[r], cx1), yy1 = tmax(s.y1[r], cy1);
-      const float xx2 = tmin(s.x2[r], cx2), yy2 = tmin(s.y2[r], cy2);
+      const float4 rb = det_box(a, pb, s.anchor[r]);
+      const float xx1 = tmax(rb.x, cx1), yy1 = tmax(rb.y, cy1);
+      const float xx2 = tmin(rb.z, cx2), yy2 = tmin(rb.w, cy2);
       float iw = __fsub_rn(xx2, xx1), ih = __fsub_rn(yy2, yy1);
       iw = iw < 0.f ? 0.f : iw;
       ih = ih < 0.f ? 0.f : ih;
       const float inter = __fmul_rn(iw, ih);
-      const float rarea = __fmul_rn(__fsub_rn(s.x2[r], s.x1[r]), __fsub_rn(s.y2[r], s.y1[r]));
+      const float rarea = __fmul_rn(__fsub_rn(rb.z, rb.x), __fsub_rn(rb.w, rb.y));
       float den = __fsub_rn(__fadd_rn(carea, rarea), inter);
       den = den < 1e-12f ? 1e-12f : den;
       const float iou = __fdiv_rn(inter, den);
@@ -224,15 +230,16 @@ __global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a) {
   __syncthreads();
 
   // 4. The first max_det kept detections, in descending score order.
-  const int kept = s_kept < a.max_det ? s_kept : a.max_det;
+  const int kept = nk;
   float* db = a.dets + b * a.ds0;
   for (int r = tid; r < kept; r += DET_THREADS) {
     const int c = s.keep[r];
     float* o = db + r * a.ds1;
-    o[0] = s.x1[c];
-    o[a.ds2] = s.y1[c];
-    o[2 * a.ds2] = s.x2[c];
-    o[3 * a.ds2] = s.y2[c];
+    const float4 box = det_box(a, pb, s.anchor[c]);
+    o[0] = box.x;
+    o[a.ds2] = box.y;
+    o[2 * a.ds2] = box.z;
+    o[3 * a.ds2] = box.w;
     o[4 * a.ds2] = s.score[c];
     o[5 * a.ds2] = (float)s.cls[c];
   }
@@ -275,8 +282,8 @@ extern "C" int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_
       dets->size[2] != 6)
     return fail(MM_ERR_INVALID, "mm_detect_nms: detections must be [B, max_det, 6]");
   if (counts == nullptr && pred->size[0] > 0) return fail(MM_ERR_INVALID, "mm_detect_nms: null counts");
-  if (pred->size[1] - 4 > 0x7fffffffLL || pred->size[0] > 0x7fffffffLL || pred->size[2] > 0x7fffffffLL)
-    return fail(MM_ERR_UNSUPPORTED, "mm_detect_nms: too large");
+  if (pred->size[1] - 4 > 32767 || pred->size[0] > 0x7fffffffLL || pred->size[2] > 0x7fffffffLL)
+    return fail(MM_ERR_UNSUPPORTED, "mm_detect_nms: too many classes, images or anchors");
   if (pred->size[0] == 0) return MM_OK;
   DetArgs a;
   a.pred = (const float*)pred->data;

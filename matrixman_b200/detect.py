@@ -22,7 +22,7 @@ import torch
 from . import _lib, ops, runtime
 from .tensor import MatrixManTensor
 
-MAX_CANDIDATES = 4096  # MM_DETECT_MAX_CANDIDATES in include/matrixman_b200.h
+MAX_CANDIDATES = 12288  # MM_DETECT_MAX_CANDIDATES in include/matrixman_b200.h
 
 
 def _check_prediction(pred) -> tuple[int, int, int]:
@@ -55,7 +55,7 @@ def postprocess_detections(pred: MatrixManTensor, width: int, height: int,
     >= ``conf_threshold``; boxes are clamped to [0, width-1] x [0, height-1];
     NMS is per class with IoU > ``iou_threshold`` suppressing.  At most
     ``max_det`` detections per image are returned, and an image may have at
-    most 4096 candidates (raise ``conf_threshold`` otherwise)."""
+    most 12288 candidates (raise ``conf_threshold`` otherwise)."""
     b, _, _ = _check_prediction(pred)
     if max_det <= 0:
         raise ValueError("MatrixMan: max_det must be positive")
@@ -76,7 +76,6 @@ def postprocess_detections(pred: MatrixManTensor, width: int, height: int,
         if n < 0:
             raise RuntimeError(f"MatrixMan: image {i} has {-n} candidates at confidence >= "
                                f"{conf_threshold}; at most {MAX_CANDIDATES} are supported")
-        rows = host[i, :n]
-        result.append([(row[:4].tolist(), float(row[4]), int(row[5]), names.get(int(row[5]), str(int(row[5]))))
-                       for row in rows])
+        result.append([(row[:4], row[4], int(row[5]), names.get(int(row[5]), str(int(row[5]))))
+                       for row in host[i, :n].tolist()])
     return result

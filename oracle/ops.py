@@ -223,3 +223,51 @@ def detections(pred: torch.Tensor, width: int, height: int, conf_threshold: floa
     sel = torch.tensor(selected, dtype=torch.long)
     sel = sel[torch.sort(conf[sel], descending=True, stable=True).indices]
     return torch.cat((conv[sel], conf[sel, None], cls[sel, None].to(torch.float32)), 1)
+
+
+def _resize_taps(dst: int, src: int, clamp_weight: bool):
+    """Source offsets and 11-bit weights of OpenCV's bilinear 8-bit resize along
+    one axis: f = float((d + 0.5) * scale - 0.5) with scale = 1 / (dst / src) in
+    double, s = floor(f), f -= s; with clamp_weight (columns) s < 0 or s >= src-1
+    clamp s with f = 0; weights round-half-even((1 - f) * 2048), (f * 2048)."""
+    scale = 1.0 / (dst / src)
+    s0 = np.zeros(dst, np.int64)
+    w = np.zeros((dst, 2), np.int64)
+    for d in range(dst):
+        f = np.float32((d + 0.5) * scale - 0.5)
+        s = int(np.floor(f))
+        f = np.float32(f - np.float32(s))
+        if clamp_weight and s < 0:
+            f, s = np.float32(0.0), 0
+        if clamp_weight and s >= src - 1:
+            f, s = np.float32(0.0), src - 1
+        s0[d] = s
+        w[d, 0] = int(np.rint(np.float32(np.float32(1.0) - f) * np.float32(2048.0)))
+        w[d, 1] = int(np.rint(f * np.float32(2048.0)))
+    return s0, w
+
+
+def resize_linear_u8(src: np.ndarray, out_h: int, out_w: int) -> np.ndarray:
+    """cv2.resize(src, (out_w, out_h), interpolation=INTER_LINEAR) for uint8
+    [H, W, C] images: OpenCV 4.x's fixed-point bilinear algorithm (the cv2 that
+    demo/yolo_helpers.py:54 calls; restated, pinned against cv2 outputs by
+    tests/golden/preprocess_vectors.npz).  Horizontal pass in integers, then
+    rows combined as ((b0*(h0>>4))>>16) + ((b1*(h1>>4))>>16) + 2) >> 2."""
+    h, w = src.shape[:2]
+    xs, xw = _resize_taps(out_w, w, True)
+    ys, yw = _resize_taps(out_h, h, False)
+    s = src.astype(np.int64)
+    x1 = np.minimum(xs + 1, w - 1)
+    hor = s[:, xs] * xw[None, :, 0, None] + s[:, x1] * xw[None, :, 1, None]
+    r0 = hor[np.clip(ys, 0, h - 1)]
+    r1 = hor[np.clip(ys + 1, 0, h - 1)]
+    b0, b1 = yw[:, 0][:, None, None], yw[:, 1][:, None, None]
+    out = (((b0 * (r0 >> 4)) >> 16) + ((b1 * (r1 >> 4)) >> 16) + 2) >> 2
+    return np.clip(out, 0, 255).astype(np.uint8)
+
+
+def preprocess_frame(frame: np.ndarray, image_size: int) -> torch.Tensor:
+    """uint8 BGR [H, W, 3] -> [1, 3, S, S] float32 RGB / 255: the reference's
+    preprocess_frame (demo/yolo_helpers.py:53-56) with the resize restated."""
+    rgb = resize_linear_u8(frame, image_size, image_size)[:, :, ::-1]
+    return torch.from_numpy(np.ascontiguousarray(rgb)).permute(2, 0, 1).contiguous().to(torch.float32).div_(255.0).unsqueeze(0)

@@ -152,3 +152,14 @@ def test_detect_reduce_oracle_semantics():
     assert r[0, :, 0].tolist() == [1.0, 2.0, 3.0, 4.0, 0.699999988079071, 1.0]
     q = torch.tensor([[[0.0], [0.0], [1.0], [1.0], [-3.0], [-2.0]]])
     assert O.detect_reduce(q)[0, 4:, 0].tolist() == [-1.0, 0.0]
+
+
+def test_preprocess_oracle_matches_reference_vectors():
+    """oracle.preprocess_frame reproduces the reference's preprocess_frame
+    (cv2 INTER_LINEAR resize, BGR -> RGB, / 255) bit for bit."""
+    d = np.load(GOLDEN / "preprocess_vectors.npz")
+    for name in ("down_wide", "up_small", "mixed", "square", "odd"):
+        size = int(d[f"size_{name}"][0])
+        got = O.preprocess_frame(d[f"frame_{name}"], size)
+        want = torch.from_numpy(d[f"rgb_{name}"]).permute(2, 0, 1).to(torch.float32).div_(255.0)[None]
+        assert bit_exact(got, want), name
