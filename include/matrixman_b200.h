@@ -395,9 +395,18 @@ int mm_detect_reduce(const mm_tensor_t* pred, const mm_tensor_t* out, void* stre
  * by anchor index).  dets [B, max_det, 6] receives the first max_det kept
  * (x1, y1, x2, y2, score, class) in descending score order and counts (device
  * int32[B]) their number; an image with more than MM_DETECT_MAX_CANDIDATES
- * candidates is skipped with counts[b] = -(candidates). */
+ * candidates is skipped with counts[b] = -(candidates).  workspace: device
+ * memory, 256-byte aligned, of at least mm_detect_nms_workspace_size bytes for
+ * this batch and anchor count (it holds the candidates between the two
+ * kernels); calls that run at the same time need separate workspaces. */
 int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_thr, float width, float height,
-                  int max_det, const mm_tensor_t* dets, int32_t* counts, void* stream);
+                  int max_det, const mm_tensor_t* dets, int32_t* counts, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* Workspace bytes mm_detect_nms needs for a [batch, 4+classes, anchors]
+ * prediction (24 bytes per anchor plus 16 per possible candidate, per image).
+ * No counterpart in the reference, whose NMS runs on the CPU. */
+int mm_detect_nms_workspace_size(int64_t batch, int64_t anchors, size_t* bytes);
 
 /* Frame preprocessing: frames (device, contiguous uint8 [n, h, w, 3] BGR) ->
  * out [n, 3, out_h, out_w] float32 RGB / 255, resized with OpenCV's 8-bit

@@ -177,7 +177,9 @@ SIGNATURES = {
     "mm_gemm": [_T, _T, _T, _d, _d, _i, _T, _vp],
     "mm_yolo_decode": [_TT, ctypes.POINTER(ctypes.c_float), _i, _i, _i, _T, _vp],
     "mm_detect_reduce": [_T, _T, _vp],
-    "mm_detect_nms": [_T, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _i, _T, _vp, _vp],
+    "mm_detect_nms": [_T, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _i, _T, _vp,
+                      _vp, ctypes.c_size_t, _vp],
+    "mm_detect_nms_workspace_size": [_i64, _i64, ctypes.POINTER(ctypes.c_size_t)],
     "mm_preprocess_bgr8": [_vp, _i64, _i64, _i64, _T, _vp],
 }
 

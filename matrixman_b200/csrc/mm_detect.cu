@@ -26,6 +26,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <string>
 
 #include "mm_common.cuh"
@@ -74,18 +75,29 @@ __global__ void detect_reduce_kernel(const float* __restrict__ pred, int64_t ps0
   }
 }
 
-// Candidate arrays in dynamic shared memory.
-struct DetSmem {
-  float* score;    // [DET_CAP]
-  int* anchor;     // [DET_CAP]
-  int16_t* cls;    // [DET_CAP]
-  int16_t* keep;   // [DET_CAP] kept candidates in order
-  int16_t* ord;    // [DET_SORT] sort order
-  uint8_t* sup;    // [DET_CAP] suppressed flags
+// Workspace of mm_detect_nms: device memory the caller provides, laid out by
+// det_work_layout (every part 256-byte aligned).
+struct DetWork {
+  float4* box;               // [B, A] clamped corner boxes of candidate anchors
+  float2* sc;                // [B, A] (best score, class as int bits) of candidate anchors
+  unsigned long long* keys;  // [B, DET_CAP] sort keys of the candidates, in arrival order
+  float* score;              // [B, DET_CAP] candidate scores in NMS order
+  int* keep;                 // [B, DET_CAP] NMS positions of the kept candidates
+  int* count;                // [B] candidates per image; zeroed before the candidate pass
 };
 
-__host__ __device__ constexpr size_t det_smem_bytes() {
-  return (size_t)DET_CAP * (4 + 4 + 2 + 2 + 1) + (size_t)DET_SORT * 2 + 64;
+__host__ __device__ inline size_t det_align(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Byte offsets of the workspace parts (DetWork order); returns the total size.
+__host__ __device__ inline size_t det_work_layout(int64_t batch, int64_t anchors, size_t off[6]) {
+  const size_t ba = (size_t)batch * (size_t)anchors, bc = (size_t)batch * DET_CAP;
+  const size_t part[6] = {ba * 16, ba * 8, bc * 8, bc * 4, bc * 4, (size_t)batch * 4};
+  size_t o = 0;
+  for (int i = 0; i < 6; ++i) {
+    off[i] = o;
+    o = det_align(o + part[i]);
+  }
+  return o;
 }
 
 // torch.maximum / torch.minimum: NaN if either operand is NaN.
@@ -110,110 +122,160 @@ __device__ __forceinline__ float4 det_box(const DetArgs& a, const float* pb, int
                      clampf_keep_nan(__fadd_rn(cx, hw), a.xmax), clampf_keep_nan(__fadd_rn(cy, hh), a.ymax));
 }
 
-// a before b in the NMS order: higher score first, then lower anchor index.
-__device__ __forceinline__ bool det_before(const DetSmem& s, int a, int b) {
-  return s.score[a] > s.score[b] || (s.score[a] == s.score[b] && s.anchor[a] < s.anchor[b]);
+// Sort key of a candidate: ascending keys = descending score, then ascending
+// anchor index.  The score's bits are mapped to an unsigned integer that
+// orders as the floats do (after -0 becomes +0, so equal scores give equal
+// high halves); NaN scores never reach here (they fail the filter).
+__device__ __forceinline__ unsigned long long det_key(float score, int anchor) {
+  unsigned u = __float_as_uint(__fadd_rn(score, 0.f));
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)(~u) << 32) | (unsigned)anchor;
 }
 
-// Sort slot x belongs strictly after slot y (-1 = padding, after every candidate).
-__device__ __forceinline__ bool det_after(const DetSmem& s, int x, int y) {
-  if (x < 0) return y >= 0;
-  if (y < 0) return false;
-  return det_before(s, y, x);
-}
-
-__global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a) {
-  extern __shared__ __align__(16) uint8_t det_raw[];
-  __shared__ int s_count;
-  DetSmem s;
-  s.score = reinterpret_cast<float*>(det_raw);
-  s.anchor = reinterpret_cast<int*>(s.score + DET_CAP);
-  s.cls = reinterpret_cast<int16_t*>(s.anchor + DET_CAP);
-  s.keep = s.cls + DET_CAP;
-  s.ord = s.keep + DET_CAP;
-  s.sup = reinterpret_cast<uint8_t*>(s.ord + DET_SORT);
-  const int64_t b = blockIdx.x;
-  const int tid = threadIdx.x;
-  if (tid == 0) s_count = 0;
-  __syncthreads();
-
-  // 1. Candidates: best class (first maximum), confidence filter, corner boxes.
-  const float* pb = a.pred + b * a.ps0;
-  for (int64_t an = tid; an < a.anchors; an += DET_THREADS) {
-    const float* p = pb + an * a.ps2;
-    float best = p[4 * a.ps1];
-    int bc = 0;
-    for (int c = 1; c < a.classes; ++c) {
-      const float v = p[(4 + c) * a.ps1];
-      if (v > best) {
-        best = v;
-        bc = c;
+// 1. Candidates, grid-wide: per anchor the best class (first maximum), the
+// confidence filter and the clamped corner box.  A candidate's box and score
+// go to the workspace at its anchor; its sort key is appended to the image's
+// key list (one atomic per warp).
+__global__ void detect_candidates_kernel(DetArgs a, DetWork w) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t b = blockIdx.y; b < a.batch; b += gridDim.y) {
+    const float* pb = a.pred + b * a.ps0;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < a.anchors;
+         base += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t an = base + threadIdx.x;
+      bool cand = false;
+      float best = 0.f;
+      int bc = 0;
+      if (an < a.anchors) {
+        const float* p = pb + an * a.ps2;
+        best = p[4 * a.ps1];
+        for (int c = 1; c < a.classes; ++c) {
+          const float v = p[(4 + c) * a.ps1];
+          if (v > best) {
+            best = v;
+            bc = c;
+          }
+        }
+        cand = best >= a.conf_thr;
       }
-    }
-    if (best >= a.conf_thr) {
-      const int slot = atomicAdd(&s_count, 1);
-      if (slot < DET_CAP) {
-        s.score[slot] = best;
-        s.cls[slot] = (int16_t)bc;
-        s.anchor[slot] = (int)an;
+      const unsigned m = __ballot_sync(0xffffffffu, cand);
+      if (m == 0u) continue;
+      const int leader = __ffs(m) - 1;
+      int slot = 0;
+      if (lane == leader) slot = atomicAdd(w.count + b, __popc(m));
+      slot = __shfl_sync(0xffffffffu, slot, leader) + __popc(m & ((1u << lane) - 1u));
+      if (cand) {
+        const int64_t i = b * a.anchors + an;
+        w.box[i] = det_box(a, pb, (int)an);
+        w.sc[i] = make_float2(best, __int_as_float(bc));
+        if (slot < DET_CAP) w.keys[b * DET_CAP + slot] = det_key(best, (int)an);
       }
     }
   }
-  __syncthreads();
-  const int count = s_count;
-  if (count > DET_CAP) {
-    if (tid == 0) a.counts[b] = -count;
+}
+
+// Shared memory of the NMS pass: the sort keys first, then (over them) the
+// boxes and classes in NMS order, a class of -1 marking a suppressed one.
+constexpr size_t DET_SMEM = (size_t)DET_CAP * (16 + 2);
+static_assert((size_t)DET_CAP * 16 >= (size_t)DET_SORT * 8, "the keys lie inside the box array");
+constexpr int DET_PER_THREAD = (DET_CAP + DET_THREADS - 1) / DET_THREADS;
+
+// 2.-4. Per image, one CTA: sort, greedy NMS, output.
+__global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a, DetWork w) {
+  extern __shared__ __align__(16) uint8_t det_raw[];
+  unsigned long long* key = reinterpret_cast<unsigned long long*>(det_raw);
+  float4* box = reinterpret_cast<float4*>(det_raw);
+  int16_t* cls = reinterpret_cast<int16_t*>(det_raw + (size_t)DET_CAP * 16);
+  const int64_t b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int n = w.count[b];
+  if (n > DET_CAP) {
+    if (tid == 0) a.counts[b] = -n;
     return;
   }
-  const int n = count;
 
-  // 2. Bitonic sort of the candidate order (padding entries sort last).
+  // 2. Bitonic sort of the keys (padding keys, all ones, sort last).
   int P = 1;
   while (P < n) P <<= 1;
-  for (int i = tid; i < P; i += DET_THREADS) {
-    s.ord[i] = (int16_t)(i < n ? i : -1);
-    if (i < n) s.sup[i] = 0;
-  }
+  const unsigned long long* kb = w.keys + b * DET_CAP;
+  for (int i = tid; i < P; i += DET_THREADS) key[i] = i < n ? kb[i] : ~0ull;
   __syncthreads();
   for (int k = 2; k <= P; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < P; i += DET_THREADS) {
-        const int l = i ^ j;
-        if (l > i) {
-          const int ai = s.ord[i], al = s.ord[l];
-          const bool up = (i & k) == 0;  // this pair's segment sorts in NMS order
-          if (up ? det_after(s, ai, al) : det_after(s, al, ai)) {
-            s.ord[i] = (int16_t)al;
-            s.ord[l] = (int16_t)ai;
-          }
+      for (int t = tid; t < (P >> 1); t += DET_THREADS) {
+        const int i = ((t & ~(j - 1)) << 1) | (t & (j - 1));  // lower slot of the pair
+        const int l = i | j;
+        const unsigned long long x = key[i], y = key[l];
+        if ((i & k) == 0 ? x > y : x < y) {
+          key[i] = y;
+          key[l] = x;
         }
       }
       __syncthreads();
     }
   }
 
+  // Boxes and classes into shared memory in NMS order (over the keys: every
+  // thread takes its keys' anchors first), scores into the workspace.
+  unsigned an[DET_PER_THREAD];
+#pragma unroll
+  for (int k = 0; k < DET_PER_THREAD; ++k) {
+    const int j = tid + k * DET_THREADS;
+    an[k] = j < n ? (unsigned)key[j] : 0u;
+  }
+  __syncthreads();
+  const float4* wb = w.box + b * a.anchors;
+  const float2* ws = w.sc + b * a.anchors;
+  float* wscore = w.score + b * DET_CAP;
+#pragma unroll
+  for (int k = 0; k < DET_PER_THREAD; ++k) {
+    const int j = tid + k * DET_THREADS;
+    if (j < n) {
+      const float2 v = ws[an[k]];
+      box[j] = wb[an[k]];
+      cls[j] = (int16_t)__float_as_int(v.y);
+      wscore[j] = v.x;
+    }
+  }
+  __syncthreads();
+
   // 3. Greedy NMS in score order, suppressing within a class only.  Kept
   // candidates are final once kept (only earlier kept ones suppress), so the
-  // pass ends after max_det of them.  nk is counted by every thread alike.
+  // pass ends after max_det of them.  i and nk are computed alike by every
+  // thread.
+  float* db = a.dets + b * a.ds0;
+  int* keep = w.keep + b * DET_CAP;
   int i = 0, nk = 0;
   while (nk < a.max_det) {
-    // uniform: every thread reads the same flags (a padding slot, which the sort
-    // never leaves among the first n, would count as suppressed)
-    while (i < n && (s.ord[i] < 0 || s.sup[s.ord[i]])) ++i;
+    // The next live position >= i: the lowest bit of a warp ballot.  Positions
+    // below it are settled, and this pass only writes positions above it.
+    while (i < n) {
+      const unsigned m = __ballot_sync(0xffffffffu, i + lane < n && cls[i + lane] >= 0);
+      if (m != 0u) {
+        i += __ffs(m) - 1;
+        break;
+      }
+      i += 32;
+    }
     if (i >= n) break;
-    const int c = s.ord[i];
-    if (tid == 0) s.keep[nk] = (int16_t)c;
+    const float4 cb = box[i];
+    const int ccls = cls[i];
+    if (tid == 0) {
+      float* o = db + (int64_t)nk * a.ds1;
+      o[0] = cb.x;
+      o[a.ds2] = cb.y;
+      o[2 * a.ds2] = cb.z;
+      o[3 * a.ds2] = cb.w;
+      o[5 * a.ds2] = (float)ccls;
+      keep[nk] = i;
+    }
     ++nk;
-    const float4 cb = det_box(a, pb, s.anchor[c]);
-    const float cx1 = cb.x, cy1 = cb.y, cx2 = cb.z, cy2 = cb.w;
-    const float carea = __fmul_rn(__fsub_rn(cx2, cx1), __fsub_rn(cy2, cy1));
-    const int ccls = s.cls[c];
+    const float carea = __fmul_rn(__fsub_rn(cb.z, cb.x), __fsub_rn(cb.w, cb.y));
     for (int j = i + 1 + tid; j < n; j += DET_THREADS) {
-      const int r = s.ord[j];
-      if (r < 0 || s.sup[r] || s.cls[r] != ccls) continue;
-      const float4 rb = det_box(a, pb, s.anchor[r]);
-      const float xx1 = tmax(rb.x, cx1), yy1 = tmax(rb.y, cy1);
-      const float xx2 = tmin(rb.z, cx2), yy2 = tmin(rb.w, cy2);
+      if (cls[j] != ccls) continue;
+      const float4 rb = box[j];
+      const float xx1 = tmax(rb.x, cb.x), yy1 = tmax(rb.y, cb.y);
+      const float xx2 = tmin(rb.z, cb.z), yy2 = tmin(rb.w, cb.w);
       float iw = __fsub_rn(xx2, xx1), ih = __fsub_rn(yy2, yy1);
       iw = iw < 0.f ? 0.f : iw;
       ih = ih < 0.f ? 0.f : ih;
@@ -222,28 +284,16 @@ __global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a) {
       float den = __fsub_rn(__fadd_rn(carea, rarea), inter);
       den = den < 1e-12f ? 1e-12f : den;
       const float iou = __fdiv_rn(inter, den);
-      if (!(iou <= a.iou_thr)) s.sup[r] = 1;
+      if (!(iou <= a.iou_thr)) cls[j] = -1;
     }
     __syncthreads();
     ++i;
   }
   __syncthreads();
 
-  // 4. The first max_det kept detections, in descending score order.
-  const int kept = nk;
-  float* db = a.dets + b * a.ds0;
-  for (int r = tid; r < kept; r += DET_THREADS) {
-    const int c = s.keep[r];
-    float* o = db + r * a.ds1;
-    const float4 box = det_box(a, pb, s.anchor[c]);
-    o[0] = box.x;
-    o[a.ds2] = box.y;
-    o[2 * a.ds2] = box.z;
-    o[3 * a.ds2] = box.w;
-    o[4 * a.ds2] = s.score[c];
-    o[5 * a.ds2] = (float)s.cls[c];
-  }
-  if (tid == 0) a.counts[b] = kept;
+  // 4. Scores of the kept detections (rows 0..nk-1 hold the rest already).
+  for (int r = tid; r < nk; r += DET_THREADS) db[(int64_t)r * a.ds1 + 4 * a.ds2] = wscore[keep[r]];
+  if (tid == 0) a.counts[b] = nk;
 }
 
 }  // namespace mm
@@ -270,9 +320,17 @@ extern "C" int mm_detect_reduce(const mm_tensor_t* pred, const mm_tensor_t* out,
   return MM_OK;
 }
 
+extern "C" int mm_detect_nms_workspace_size(int64_t batch, int64_t anchors, size_t* bytes) {
+  if (bytes == nullptr || batch < 0 || anchors < 0)
+    return fail(MM_ERR_INVALID, "mm_detect_nms_workspace_size: bad arguments");
+  size_t off[6];
+  *bytes = det_work_layout(batch, anchors, off);
+  return MM_OK;
+}
+
 extern "C" int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_thr, float width,
                              float height, int max_det, const mm_tensor_t* dets, int32_t* counts,
-                             void* stream) {
+                             void* workspace, size_t workspace_bytes, void* stream) {
   int rc;
   if ((rc = validate(pred, "mm_detect_nms prediction", MM_F32)) != MM_OK) return rc;
   if ((rc = validate(dets, "mm_detect_nms detections", MM_F32)) != MM_OK) return rc;
@@ -285,6 +343,12 @@ extern "C" int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_
   if (pred->size[1] - 4 > 32767 || pred->size[0] > 0x7fffffffLL || pred->size[2] > 0x7fffffffLL)
     return fail(MM_ERR_UNSUPPORTED, "mm_detect_nms: too many classes, images or anchors");
   if (pred->size[0] == 0) return MM_OK;
+  size_t off[6];
+  const size_t need = det_work_layout(pred->size[0], pred->size[2], off);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(MM_ERR_INVALID, "mm_detect_nms: workspace smaller than mm_detect_nms_workspace_size");
+  if (((uintptr_t)workspace & 255u) != 0u)
+    return fail(MM_ERR_INVALID, "mm_detect_nms: workspace must be 256-byte aligned");
   DetArgs a;
   a.pred = (const float*)pred->data;
   a.ps0 = pred->stride[0]; a.ps1 = pred->stride[1]; a.ps2 = pred->stride[2];
@@ -299,20 +363,32 @@ extern "C" int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_
   a.dets = (float*)dets->data;
   a.ds0 = dets->stride[0]; a.ds1 = dets->stride[1]; a.ds2 = dets->stride[2];
   a.counts = counts;
-  const size_t smem = det_smem_bytes();
+  uint8_t* base = (uint8_t*)workspace;
+  DetWork w;
+  w.box = (float4*)(base + off[0]);
+  w.sc = (float2*)(base + off[1]);
+  w.keys = (unsigned long long*)(base + off[2]);
+  w.score = (float*)(base + off[3]);
+  w.keep = (int*)(base + off[4]);
+  w.count = (int*)(base + off[5]);
   {
     static bool configured[256] = {};
     int dev = 0;
     MM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
     if (dev >= 0 && dev < 256 && !configured[dev]) {
       MM_CUDA(cudaFuncSetAttribute(detect_nms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)smem),
+                                   (int)DET_SMEM),
               "mm_detect_nms: shared memory attribute");
       configured[dev] = true;
     }
   }
   cudaStream_t s = resolve_stream(stream);
-  detect_nms_kernel<<<(unsigned)a.batch, DET_THREADS, smem, s>>>(a);
+  MM_CUDA(cudaMemsetAsync(w.count, 0, (size_t)a.batch * sizeof(int), s), "mm_detect_nms: clear counts");
+  const int64_t xblocks = std::min<int64_t>((a.anchors + 255) / 256, 1024);
+  const dim3 grid((unsigned)std::max<int64_t>(xblocks, 1), (unsigned)std::min<int64_t>(a.batch, 65535));
+  detect_candidates_kernel<<<grid, 256, 0, s>>>(a, w);
+  MM_LAUNCH_CHECK("mm_detect_nms candidate launch");
+  detect_nms_kernel<<<(unsigned)a.batch, DET_THREADS, DET_SMEM, s>>>(a, w);
   MM_LAUNCH_CHECK("mm_detect_nms launch");
   return MM_OK;
 }

@@ -62,9 +62,14 @@ def postprocess_detections(pred: MatrixManTensor, width: int, height: int,
     rt = pred.runtime
     dets = ops.empty(rt, (b, int(max_det), 6))
     counts = rt.new_storage(max(b, 1), torch.int32)
+    ws_bytes = ctypes.c_size_t(0)
+    _lib.check(rt.lib.mm_detect_nms_workspace_size(b, int(pred.shape[2]), ctypes.byref(ws_bytes)),
+               "detection workspace size")
+    work = rt.new_storage(max(ws_bytes.value, 1), torch.uint8)
     ops._launch("mm_detect_nms", ops._p(pred.desc()), float(conf_threshold), float(iou_threshold),
                 float(width), float(height), int(max_det), ops._p(dets.desc()),
-                ctypes.c_void_p(counts.pointer), rt.stream)
+                ctypes.c_void_p(counts.pointer), ctypes.c_void_p(work.pointer), ws_bytes.value,
+                rt.stream)
     host_counts = torch.empty(b, dtype=torch.int32)
     if b:
         rt.download(counts.pointer, host_counts)
