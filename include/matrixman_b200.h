@@ -408,6 +408,26 @@ int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_thr, float 
  * No counterpart in the reference, whose NMS runs on the CPU. */
 int mm_detect_nms_workspace_size(int64_t batch, int64_t anchors, size_t* bytes);
 
+/* Scratch size behind mm_detect_nms_static, fixed per GPU: 4 MiB, enough for
+ * 10 images of 640 x 640 (8400 anchors) in one call. */
+#define MM_DETECT_STATIC_WORK_BYTES (4u << 20)
+
+/* mm_detect_nms for callers that cannot allocate device memory: a plugin
+ * inside an application that owns all GPU memory and forbids cudaMalloc after
+ * start-up, or a real-time loop whose memory is fixed before it runs.  It
+ * takes no workspace and allocates nothing; its scratch is a static device
+ * array of MM_DETECT_STATIC_WORK_BYTES that every GPU loading the library
+ * holds until the process exits.  Same arguments and results as mm_detect_nms
+ * otherwise.  A call whose batch needs more scratch (see
+ * mm_detect_nms_workspace_size) fails with MM_ERR_UNSUPPORTED.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  All calls on a device share the
+ * array: calls that overlap on the GPU (other streams, other host threads)
+ * race, so serialise them.  No counterpart in the reference. */
+int mm_detect_nms_static(const mm_tensor_t* pred, float conf_thr, float iou_thr, float width,
+                         float height, int max_det, const mm_tensor_t* dets, int32_t* counts,
+                         void* stream);
+
 /* Frame preprocessing: frames (device, contiguous uint8 [n, h, w, 3] BGR) ->
  * out [n, 3, out_h, out_w] float32 RGB / 255, resized with OpenCV's 8-bit
  * INTER_LINEAR fixed-point bilinear algorithm.  Replaces the reference's CPU

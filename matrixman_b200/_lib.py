@@ -180,6 +180,8 @@ SIGNATURES = {
     "mm_detect_nms": [_T, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _i, _T, _vp,
                       _vp, ctypes.c_size_t, _vp],
     "mm_detect_nms_workspace_size": [_i64, _i64, ctypes.POINTER(ctypes.c_size_t)],
+    "mm_detect_nms_static": [_T, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _i, _T,
+                             _vp, _vp],
     "mm_preprocess_bgr8": [_vp, _i64, _i64, _i64, _T, _vp],
 }
 

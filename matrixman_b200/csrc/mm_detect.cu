@@ -27,6 +27,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 
 #include "mm_common.cuh"
@@ -391,4 +392,53 @@ extern "C" int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_
   detect_nms_kernel<<<(unsigned)a.batch, DET_THREADS, DET_SMEM, s>>>(a, w);
   MM_LAUNCH_CHECK("mm_detect_nms launch");
   return MM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// mm_detect_nms_static: the same detection NMS for callers that may not
+// allocate device memory -- a plugin inside a host application that owns all
+// GPU memory and forbids cudaMalloc after start-up, or a real-time loop whose
+// memory is fixed before it starts.  Its workspace is this file's static device
+// array instead of a caller buffer.  Every GPU that loads the library holds
+// the array until the process exits, and all calls on a GPU share it.
+static __device__ __align__(256) uint8_t det_static_work[MM_DETECT_STATIC_WORK_BYTES];
+
+namespace {
+std::mutex det_static_mu;
+void* det_static_addr[256] = {};  // device address of det_static_work, per device
+}  // namespace
+
+extern "C" int mm_detect_nms_static(const mm_tensor_t* pred, float conf_thr, float iou_thr,
+                                    float width, float height, int max_det, const mm_tensor_t* dets,
+                                    int32_t* counts, void* stream) {
+  int rc;
+  if ((rc = validate(pred, "mm_detect_nms_static prediction", MM_F32)) != MM_OK) return rc;
+  if (pred->ndim == 3 && pred->size[0] > 0) {
+    size_t off[6];
+    const size_t need = det_work_layout(pred->size[0], pred->size[2], off);
+    if (need > (size_t)MM_DETECT_STATIC_WORK_BYTES)
+      return fail(MM_ERR_UNSUPPORTED,
+                  "mm_detect_nms_static: " + std::to_string(pred->size[0]) + " images of " +
+                      std::to_string(pred->size[2]) + " anchors need " + std::to_string(need) +
+                      " bytes of scratch, more than its fixed " +
+                      std::to_string((size_t)MM_DETECT_STATIC_WORK_BYTES) +
+                      "; split the batch or call mm_detect_nms with a workspace");
+  }
+  int dev = 0;
+  MM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 256) return fail(MM_ERR_UNSUPPORTED, "mm_detect_nms_static: device index above 255");
+  void* work = nullptr;
+  {
+    // First call on a device: the array's device address (the name itself is
+    // only a host-side stand-in).
+    std::lock_guard<std::mutex> lock(det_static_mu);
+    if (det_static_addr[dev] == nullptr) {
+      void* addr = nullptr;
+      MM_CUDA(cudaGetSymbolAddress(&addr, det_static_work), "mm_detect_nms_static: static scratch address");
+      det_static_addr[dev] = addr;
+    }
+    work = det_static_addr[dev];
+  }
+  return mm_detect_nms(pred, conf_thr, iou_thr, width, height, max_det, dets, counts, work,
+                       (size_t)MM_DETECT_STATIC_WORK_BYTES, stream);
 }
