@@ -295,6 +295,42 @@ int mm_batch_norm(const mm_tensor_t* x, const float* mean, const float* var, con
  * (gpumatrix.py:784-931) and CudaBackend.softmax (cuda/backend.py:1290-1349). */
 int mm_softmax(const mm_tensor_t* x, int dim, int log, const mm_tensor_t* y, void* stream);
 
+/* Training-path ops (backward passes and Adam's update).  The reference has
+ * them on its OpenGL backend only: backends/opengl/dispatch.py:171-179
+ * (lerp_), :264-290 (addcmul_, addcdiv_), :299 (sqrt), :377-382
+ * (threshold_backward), :463-479 (log-softmax backward, NLL forward and
+ * backward). */
+enum {
+  MM_PW3_THRESHOLD_BACKWARD = 0, /* y = a <= s ? 0 : x   (x = grad, a = self) */
+  MM_PW3_ADDCMUL = 1,            /* y = fma(s * a, b, x) */
+  MM_PW3_ADDCDIV = 2,            /* y = x + (s * a) / b */
+  MM_PW3_LERP = 3,               /* y = lerp(x, a, weight s); b unused */
+  MM_PW3_SQRT = 4                /* y = sqrt(x); a, b unused */
+};
+
+/* Element-wise op over x, a, b (same shape as y, any strides; y may be x). */
+int mm_pointwise3(int op, const mm_tensor_t* x, const mm_tensor_t* a, const mm_tensor_t* b,
+                  const mm_tensor_t* y, double s, void* stream);
+
+/* _log_softmax_backward_data: y = grad - exp(output) * sum(grad along dim);
+ * contiguous operands. */
+int mm_log_softmax_backward(const mm_tensor_t* grad, const mm_tensor_t* output, int dim,
+                            const mm_tensor_t* y, void* stream);
+
+/* nll_loss_forward: input [N, C] f32 (log-probabilities), target [N] int64,
+ * weight [C] or NULL; reduction 0 none (out [N]), 1 mean, 2 sum (out and
+ * total_weight hold one value).  Rows whose target is ignore_index are
+ * skipped; targets must otherwise lie in [0, C) (the caller checks). */
+int mm_nll_loss(const mm_tensor_t* input, const mm_tensor_t* target, const mm_tensor_t* weight,
+                int reduction, int64_t ignore_index, const mm_tensor_t* out,
+                const mm_tensor_t* total_weight, void* stream);
+
+/* nll_loss_backward into a contiguous grad_input [N, C] (zeroed here). */
+int mm_nll_loss_backward(const mm_tensor_t* grad_output, const mm_tensor_t* input,
+                         const mm_tensor_t* target, const mm_tensor_t* weight, int reduction,
+                         int64_t ignore_index, const mm_tensor_t* total_weight,
+                         const mm_tensor_t* grad_input, void* stream);
+
 /* Generic 2-D max pooling over dims (2,3) of a rank-4 tensor, -inf padding,
  * NaN-propagating like torch.  Replaces max_pool2d_5x5_s1_p2 (gpumatrix.py:74)
  * and CudaBackend.max_pool2d (cuda/backend.py:1351-1393), which only accepted

@@ -34,6 +34,7 @@ ACT_NONE, ACT_RELU, ACT_SILU, ACT_SIGMOID = 0, 1, 2, 3
 (UNARY_COPY, UNARY_SILU, UNARY_RELU, UNARY_SIGMOID, UNARY_ADD_SCALAR, UNARY_MUL_SCALAR,
  UNARY_DIV_SCALAR, UNARY_NEG, UNARY_CLAMP) = range(9)
 BINARY_ADD, BINARY_SUB, BINARY_MUL, BINARY_DIV = range(4)
+PW3_THRESHOLD_BACKWARD, PW3_ADDCMUL, PW3_ADDCDIV, PW3_LERP, PW3_SQRT = range(5)
 
 LIB_DIR = Path(__file__).resolve().parent / "_lib"
 LIB_PATH = LIB_DIR / "libmatrixman_b200.so"
@@ -183,6 +184,10 @@ SIGNATURES = {
     "mm_detect_nms_static": [_T, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _i, _T,
                              _vp, _vp],
     "mm_preprocess_bgr8": [_vp, _i64, _i64, _i64, _T, _vp],
+    "mm_pointwise3": [_i, _T, _T, _T, _T, _d, _vp],
+    "mm_log_softmax_backward": [_T, _T, _i, _T, _vp],
+    "mm_nll_loss": [_T, _T, _T, _i, _i64, _T, _T, _vp],
+    "mm_nll_loss_backward": [_T, _T, _T, _T, _i, _i64, _T, _T, _vp],
 }
 
 

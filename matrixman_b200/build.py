@@ -39,7 +39,7 @@ NVCC_FLAGS = [
     f"-I{ROOT / 'include'}",
 ]
 
-SOURCES = ["mm_runtime.cu", "mm_ops.cu", "mm_conv_simt.cu", "mm_conv_tc.cu", "mm_detect.cu", "mm_frames.cu"]
+SOURCES = ["mm_runtime.cu", "mm_ops.cu", "mm_conv_simt.cu", "mm_conv_tc.cu", "mm_detect.cu", "mm_frames.cu", "mm_train.cu"]
 
 
 def _digest(paths) -> str:

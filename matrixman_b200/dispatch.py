@@ -322,6 +322,89 @@ def _log_softmax(x, dim, half_to_float=False):
     return ops.softmax(x, dim, log=True)
 
 
+# -- training path (backward passes, Adam's update) --------------------------
+from . import _lib as _native_lib  # noqa: E402
+
+
+def _scalar_arg(v, op):
+    if isinstance(v, torch.Tensor) and not isinstance(v, MatrixManTensor) and v.numel() == 1:
+        return float(v.item())
+    if isinstance(v, (int, float, bool)):
+        return float(v)
+    raise RuntimeError(f"MatrixMan/CUDA: {op} needs a numeric scalar")
+
+
+@_register(aten.threshold_backward.default)
+def _threshold_backward(grad_output, self, threshold):
+    if tuple(grad_output.shape) != tuple(self.shape):
+        raise RuntimeError("MatrixMan/CUDA: threshold_backward requires equal shapes")
+    return ops.pointwise3(_native_lib.PW3_THRESHOLD_BACKWARD, grad_output, self, grad_output,
+                          _scalar_arg(threshold, "threshold_backward"), name="threshold_backward")
+
+
+@_register(aten._log_softmax_backward_data.default)
+def _log_softmax_backward(grad_output, output, dim, input_dtype):
+    return ops.log_softmax_backward(grad_output, output, dim)
+
+
+@_register(aten.nll_loss_forward.default)
+def _nll_loss_forward(self, target, weight, reduction, ignore_index):
+    return ops.nll_loss(self, target, weight, reduction, ignore_index)
+
+
+@_register(aten.nll_loss_backward.default)
+def _nll_loss_backward(grad_output, self, target, weight, reduction, ignore_index, total_weight):
+    return ops.nll_loss_backward(grad_output, self, target, weight, reduction, ignore_index, total_weight)
+
+
+def _pw3_inplace(code, self, a, b, s, name):
+    return ops.pointwise3(code, self, a, b, s, out=self, name=name)
+
+
+@_register(aten.addcmul.default)
+def _addcmul(self, tensor1, tensor2, *, value=1):
+    return ops.pointwise3(_native_lib.PW3_ADDCMUL, self, tensor1, tensor2, _scalar_arg(value, "addcmul"),
+                          name="addcmul")
+
+
+@_register(aten.addcmul_.default)
+def _addcmul_(self, tensor1, tensor2, *, value=1):
+    return _pw3_inplace(_native_lib.PW3_ADDCMUL, self, tensor1, tensor2, _scalar_arg(value, "addcmul_"),
+                        "addcmul_")
+
+
+@_register(aten.addcdiv.default)
+def _addcdiv(self, tensor1, tensor2, *, value=1):
+    return ops.pointwise3(_native_lib.PW3_ADDCDIV, self, tensor1, tensor2, _scalar_arg(value, "addcdiv"),
+                          name="addcdiv")
+
+
+@_register(aten.addcdiv_.default)
+def _addcdiv_(self, tensor1, tensor2, *, value=1):
+    return _pw3_inplace(_native_lib.PW3_ADDCDIV, self, tensor1, tensor2, _scalar_arg(value, "addcdiv_"),
+                        "addcdiv_")
+
+
+@_register(aten.lerp.Scalar)
+def _lerp(self, end, weight):
+    return ops.pointwise3(_native_lib.PW3_LERP, self, end, None, _scalar_arg(weight, "lerp"), name="lerp")
+
+
+@_register(aten.lerp_.Scalar)
+def _lerp_(self, end, weight):
+    return _pw3_inplace(_native_lib.PW3_LERP, self, end, None, _scalar_arg(weight, "lerp_"), "lerp_")
+
+
+@_register(aten.sqrt.default)
+def _sqrt(self):
+    return ops.pointwise3(_native_lib.PW3_SQRT, self, name="sqrt")
+
+
+@_register(aten.sqrt_.default)
+def _sqrt_(self):
+    return _pw3_inplace(_native_lib.PW3_SQRT, self, None, None, 0.0, "sqrt_")
+
+
 @_register(aten.relu.default)
 def _relu(x):
     return ops.unary("relu", x)
@@ -543,6 +626,12 @@ def _new_ones(x, size, dtype=None, layout=None, device=None, pin_memory=None):
 def _new_empty(x, size, dtype=None, layout=None, device=None, pin_memory=None):
     rt = _factory_runtime(x, device)
     return ops.empty(rt, tuple(int(s) for s in size), None, _check_dtype(dtype, x))
+
+
+@_register(aten.new_empty_strided.default)
+def _new_empty_strided(x, size, stride, dtype=None, layout=None, device=None, pin_memory=None):
+    rt = _factory_runtime(x, device)
+    return ops.empty(rt, tuple(int(s) for s in size), tuple(int(s) for s in stride), _check_dtype(dtype, x))
 
 
 @_register(aten.empty_like.default)

@@ -26,6 +26,7 @@ from .tensor import (
     is_channels_last,
     is_dense,
     numel,
+    readback_tensor,
 )
 
 F32 = torch.float32
@@ -643,3 +644,109 @@ def upsample_nearest2d(x, output_size, scales_h=None, scales_w=None) -> MatrixMa
     _launch("mm_upsample_nearest2d", _p(x.desc()), float(scales_h or 0.0), float(scales_w or 0.0),
             _p(y.desc()), _stream(x))
     return y
+
+
+# ---------------------------------------------------------------------------
+# Training path: backward passes and Adam's element-wise update (the reference
+# has these on its OpenGL backend only, backends/opengl/dispatch.py:171-179,
+# :264-290, :299, :377-382, :463-479).
+# ---------------------------------------------------------------------------
+def pointwise3(code: int, x, a=None, b=None, scalar=0.0, out: MatrixManTensor | None = None,
+               name: str = "pointwise") -> MatrixManTensor:
+    """y = op(x, a, b; scalar), a and b broadcast; ``out`` may be ``x`` (in-place)."""
+    x = require_mm(x, name)
+    a = x if a is None else require_mm(a, name)
+    b = x if b is None else require_mm(b, name)
+    for t in (x, a, b):
+        require_f32(t, name)
+    _runtime_of(x, a, b)
+    shape = broadcast_shapes(broadcast_shapes(tuple(x.shape), tuple(a.shape)), tuple(b.shape))
+    if out is not None and tuple(out.shape) != shape:
+        raise RuntimeError(f"MatrixMan/CUDA: {name}: output with shape {tuple(out.shape)} doesn't "
+                           f"match the broadcast shape {shape}")
+    y = out if out is not None else (empty_like(x) if tuple(x.shape) == shape else empty(x.runtime, shape))
+    ex, ea, eb = (expand_view(t, shape) if tuple(t.shape) != shape else t for t in (x, a, b))
+    _launch("mm_pointwise3", int(code), _p(ex.desc()), _p(ea.desc()), _p(eb.desc()), _p(y.desc()),
+            float(scalar), _stream(x))
+    return y
+
+
+def log_softmax_backward(grad, output, dim) -> MatrixManTensor:
+    grad = require_mm(grad, "log_softmax_backward")
+    output = require_mm(output, "log_softmax_backward")
+    require_f32(grad, "log_softmax_backward")
+    require_f32(output, "log_softmax_backward")
+    if tuple(grad.shape) != tuple(output.shape):
+        raise RuntimeError("MatrixMan/CUDA: log_softmax_backward needs equal shapes")
+    rank = grad.dim()
+    d = int(dim) + (rank if int(dim) < 0 else 0)
+    if rank and not 0 <= d < rank:
+        raise IndexError("MatrixMan/CUDA: log_softmax_backward dimension is out of range")
+    dense = contiguous_strides(tuple(grad.shape))
+    g = grad if tuple(grad._logical_strides) == dense else materialize(grad)
+    o = output if tuple(output._logical_strides) == dense else materialize(output)
+    y = empty(grad.runtime, tuple(grad.shape))
+    _launch("mm_log_softmax_backward", _p(g.desc()), _p(o.desc()), max(d, 0), _p(y.desc()), _stream(grad))
+    return y
+
+
+_REDUCTIONS = (0, 1, 2)
+
+
+def _nll_operands(x, target, weight, reduction, ignore_index, op):
+    x = require_mm(x, op)
+    require_f32(x, op)
+    if x.dim() != 2:
+        raise NotImplementedError(f"MatrixMan/CUDA: {op} supports input [N, C] and target [N]")
+    if int(reduction) not in _REDUCTIONS:
+        raise RuntimeError(f"MatrixMan/CUDA: {op} unsupported reduction={reduction}")
+    rt = x.runtime
+    if isinstance(target, MatrixManTensor):
+        host_target = None
+    elif isinstance(target, torch.Tensor) and target.device.type == "cpu":
+        host_target = target
+    else:
+        raise RuntimeError(f"MatrixMan/CUDA: {op} requires a tensor target")
+    if target.dtype != torch.int64 or target.dim() != 1 or target.shape[0] != x.shape[0]:
+        raise RuntimeError(f"MatrixMan/CUDA: {op} requires an int64 target [N] for input [N, C]")
+    if host_target is not None:
+        target = MatrixManTensor(rt.upload(host_target.contiguous()), tuple(host_target.shape), 0,
+                                 contiguous_strides(tuple(host_target.shape)))
+    w = None
+    if weight is not None:
+        w = device_operand(rt, weight, f"{op} weight")
+        if tuple(w.shape) != (int(x.shape[1]),):
+            raise RuntimeError(f"MatrixMan/CUDA: {op} weight must be [C]")
+    return x, target, w, host_target
+
+
+def _check_targets(values: torch.Tensor, classes: int, ignore_index: int, op: str) -> None:
+    bad = (values != int(ignore_index)) & ((values < 0) | (values >= classes))
+    if bool(bad.any()):
+        raise RuntimeError(f"MatrixMan/CUDA: {op} target contains an out-of-range class index")
+
+
+def nll_loss(x, target, weight=None, reduction=1, ignore_index=-100):
+    """nll_loss_forward: (output, total_weight).  Targets are checked on the
+    host (a device target is read back first), as the reference does."""
+    x, target, w, host_target = _nll_operands(x, target, weight, reduction, ignore_index, "nll_loss_forward")
+    values = host_target if host_target is not None else readback_tensor(target)
+    _check_targets(values, int(x.shape[1]), ignore_index, "nll_loss_forward")
+    rt = x.runtime
+    total = full(rt, (), 0.0)
+    out = empty(rt, (int(x.shape[0]),) if int(reduction) == 0 else ())
+    _launch("mm_nll_loss", _p(x.desc()), _p(target.desc()), _p(w.desc()) if w is not None else None,
+            int(reduction), int(ignore_index), _p(out.desc()), _p(total.desc()), _stream(x))
+    return out, total
+
+
+def nll_loss_backward(grad_output, x, target, weight, reduction, ignore_index, total_weight):
+    x, target, w, _ = _nll_operands(x, target, weight, reduction, ignore_index, "nll_loss_backward")
+    rt = x.runtime
+    go = device_operand(rt, grad_output, "nll_loss_backward grad_output")
+    tw = device_operand(rt, total_weight, "nll_loss_backward total_weight")
+    gi = empty(rt, tuple(x.shape))
+    _launch("mm_nll_loss_backward", _p(go.desc()), _p(x.desc()), _p(target.desc()),
+            _p(w.desc()) if w is not None else None, int(reduction), int(ignore_index), _p(tw.desc()),
+            _p(gi.desc()), _stream(x))
+    return gi
