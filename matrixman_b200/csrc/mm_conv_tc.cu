@@ -44,6 +44,7 @@
 #include <stdint.h>
 
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -793,6 +794,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: the set-up above (barriers, TMEM, bias, all
+  // independent of earlier kernels' results) overlaps the previous kernel's
+  // tail; the next convolution may be scheduled from here on (its CTAs take an
+  // SM only as one of ours leaves, one CTA per SM), and nothing below reads an
+  // input or writes the output before every earlier kernel has completed.
+  // Both instructions do nothing in a launch without the attribute.
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // TMEM columns: lo stages at [32 s, 32 s + 32); from acc0 = 32 S two period
   // buffers of 2 bn columns ([hi*hi | hi*lo], [acc0, acc0 + 4 bn)), then xbuf
   // lo*hi tile sums of bn columns.
@@ -1515,9 +1524,24 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
     if (smem < min_smem[dev][variant]) smem = min_smem[dev][variant];
     if (smem > configured[dev][variant]) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: shared memory");
   }
-  // Persistent CTAs: one per SM.
+  // Persistent CTAs: one per SM.  Launched as a programmatic dependent of the
+  // previous kernel in the stream unless MATRIXMAN_CONV_PDL=0.
   const int64_t ctas = a.tiles < (int64_t)sm_count() ? a.tiles : (int64_t)sm_count();
-  kernel<<<(unsigned)ctas, TC_THREADS, smem, resolve_stream(stream)>>>(mhi, mlo, amap, ymap, a);
+  static const bool pdl = [] {
+    const char* env = std::getenv("MATRIXMAN_CONV_PDL");
+    return !(env != nullptr && env[0] == '0');
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = resolve_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  MM_CUDA(cudaLaunchKernelEx(&cfg, kernel, mhi, mlo, amap, ymap, a), "mm_conv2d_tc launch");
   MM_LAUNCH_CHECK("mm_conv2d_tc launch");
   return MM_OK;
 }
