@@ -78,3 +78,29 @@ def test_yolo_output_postprocessed_on_device(mm, batch, size):
     for i in range(batch):
         want = O.detections(host[i], size, size, 0.3, 0.5)
         assert bit_exact(as_tensor(got[i]), want)
+
+
+def test_nms_workspace_contract(mm):
+    """mm_detect_nms rejects a workspace that is too small or not 256-byte
+    aligned (host-side checks, before any launch); max_det = 0 keeps nothing."""
+    import ctypes
+    from matrixman_b200 import _lib, ops
+    pred = mm.to_device(torch.rand(2, 6, 500, generator=gen(3)))
+    rt = pred.runtime
+    need = ctypes.c_size_t(0)
+    _lib.check(rt.lib.mm_detect_nms_workspace_size(2, 500, ctypes.byref(need)))
+    work = rt.new_storage(need.value + 256, torch.uint8)
+    counts = rt.new_storage(2, torch.int32)
+
+    def call(max_det, ptr, nbytes):
+        dets = ops.empty(rt, (2, max_det, 6))
+        return rt.lib.mm_detect_nms(ops._p(pred.desc()), 0.25, 0.45, 640.0, 640.0, max_det,
+                                    ops._p(dets.desc()), ctypes.c_void_p(counts.pointer),
+                                    ctypes.c_void_p(ptr), nbytes, rt.stream)
+
+    assert call(5, work.pointer, need.value - 1) == _lib.MM_ERR_INVALID
+    assert call(5, work.pointer + 16, need.value) == _lib.MM_ERR_INVALID
+    assert call(0, work.pointer, need.value) == _lib.MM_OK
+    host = torch.full((2,), -7, dtype=torch.int32)
+    rt.download(counts.pointer, host)
+    assert host.tolist() == [0, 0]
