@@ -19,7 +19,7 @@ import ctypes
 
 import torch
 
-from . import _lib, ops, runtime
+from . import _lib, audit, ops, runtime
 from .tensor import MatrixManTensor
 
 MAX_CANDIDATES = 12288  # MM_DETECT_MAX_CANDIDATES in include/matrixman_b200.h
@@ -60,24 +60,29 @@ def postprocess_detections(pred: MatrixManTensor, width: int, height: int,
     if max_det <= 0:
         raise ValueError("MatrixMan: max_det must be positive")
     rt = pred.runtime
-    dets = ops.empty(rt, (b, int(max_det), 6))
-    counts = rt.new_storage(max(b, 1), torch.int32)
+    # One block holds the detections and, after them, the per-image counts
+    # (int32), so a single copy reads both back.
+    n_det = b * int(max_det) * 6
+    block = rt.new_storage(n_det + max(b, 1), torch.float32)
+    dets = MatrixManTensor._from_owner(block, (b, int(max_det), 6), 0, (int(max_det) * 6, 6, 1))
     ws_bytes = ctypes.c_size_t(0)
     _lib.check(rt.lib.mm_detect_nms_workspace_size(b, int(pred.shape[2]), ctypes.byref(ws_bytes)),
                "detection workspace size")
     work = rt.new_storage(max(ws_bytes.value, 1), torch.uint8)
     ops._launch("mm_detect_nms", ops._p(pred.desc()), float(conf_threshold), float(iou_threshold),
                 float(width), float(height), int(max_det), ops._p(dets.desc()),
-                ctypes.c_void_p(counts.pointer), ctypes.c_void_p(work.pointer), ws_bytes.value,
+                ctypes.c_void_p(block.pointer + n_det * 4), ctypes.c_void_p(work.pointer), ws_bytes.value,
                 rt.stream)
-    host_counts = torch.empty(b, dtype=torch.int32)
+    flat = torch.empty(n_det + b, dtype=torch.float32)
     if b:
-        rt.download(counts.pointer, host_counts)
-    host = dets.cpu()
+        rt.download(block.pointer, flat)
+    audit.record("explicit_readback", flat)
+    host_counts = flat[n_det:].view(torch.int32).tolist()
+    host = flat[:n_det].view(b, int(max_det), 6)
     names = names or {}
     result = []
     for i in range(b):
-        n = int(host_counts[i])
+        n = host_counts[i]
         if n < 0:
             raise RuntimeError(f"MatrixMan: image {i} has {-n} candidates at confidence >= "
                                f"{conf_threshold}; at most {MAX_CANDIDATES} are supported")
