@@ -5,6 +5,8 @@
 #include <stdint.h>
 
 #include <cstdio>
+#include <cstdlib>
+#include <utility>
 #include <string>
 
 #include "../../include/matrixman_b200.h"
@@ -30,6 +32,39 @@ int cuda_fail(cudaError_t err, const char* action);
   } while (0)
 
 cudaStream_t resolve_stream(void* stream);
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL).  A kernel launched with launch_pdl may
+// be scheduled while the previous kernel in the stream drains; it must call
+// pdl_wait() before its first global-memory access, which returns once every
+// earlier kernel has completed and its writes are visible (a no-op in a launch
+// without the attribute).  MATRIXMAN_PDL=0 launches everything plainly.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* env = std::getenv("MATRIXMAN_PDL");
+    return !(env != nullptr && env[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Number of SMs of the current device (cached per device).
 int sm_count();

@@ -249,6 +249,7 @@ __device__ __forceinline__ float act_fast(float v, int act) {
 
 template <int CIN, int R, int S>
 __global__ void __launch_bounds__(128) conv_smallc_kernel(ConvArgs a, int vec_store) {
+  pdl_wait();
   __shared__ float4 wsm[CIN * R * S * (SC_KT / 4)];
   const int k0 = blockIdx.y * SC_KT;
   for (int i = threadIdx.x; i < CIN * R * S * SC_KT; i += blockDim.x) {
@@ -328,7 +329,8 @@ int launch_smallc(const ConvArgs& a, int vec_store, cudaStream_t s) {
   const int64_t cap = (int64_t)sm_count() * 16;
   if (blocks > cap) blocks = cap;
   dim3 grid((unsigned)blocks, (unsigned)((a.kout + SC_KT - 1) / SC_KT));
-  conv_smallc_kernel<CIN, R, S><<<grid, 128, 0, s>>>(a, vec_store);
+  MM_CUDA(launch_pdl(conv_smallc_kernel<CIN, R, S>, grid, dim3(128), 0, s, a, vec_store),
+          "mm_conv2d small-channel launch");
   MM_LAUNCH_CHECK("mm_conv2d small-channel launch");
   return MM_OK;
 }

@@ -1524,24 +1524,12 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
     if (smem < min_smem[dev][variant]) smem = min_smem[dev][variant];
     if (smem > configured[dev][variant]) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: shared memory");
   }
-  // Persistent CTAs: one per SM.  Launched as a programmatic dependent of the
-  // previous kernel in the stream unless MATRIXMAN_CONV_PDL=0.
+  // Persistent CTAs: one per SM, launched as a programmatic dependent of the
+  // previous kernel in the stream (launch_pdl).
   const int64_t ctas = a.tiles < (int64_t)sm_count() ? a.tiles : (int64_t)sm_count();
-  static const bool pdl = [] {
-    const char* env = std::getenv("MATRIXMAN_CONV_PDL");
-    return !(env != nullptr && env[0] == '0');
-  }();
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)ctas);
-  cfg.blockDim = dim3(TC_THREADS);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = resolve_stream(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  MM_CUDA(cudaLaunchKernelEx(&cfg, kernel, mhi, mlo, amap, ymap, a), "mm_conv2d_tc launch");
+  MM_CUDA(launch_pdl(kernel, dim3((unsigned)ctas), dim3(TC_THREADS), smem, resolve_stream(stream), mhi, mlo,
+                     amap, ymap, a),
+          "mm_conv2d_tc launch");
   MM_LAUNCH_CHECK("mm_conv2d_tc launch");
   return MM_OK;
 }

@@ -162,6 +162,7 @@ __global__ void copy_strided_kernel(const T* __restrict__ x, T* __restrict__ y, 
 // has four independent loads in flight before its stores.
 __global__ void copy_rows_vec4_kernel(const float* __restrict__ x, float* __restrict__ y,
                                       int64_t rows, int cols4, int64_t xs, int64_t ys) {
+  pdl_wait();
   const int64_t total = rows * cols4;
   const int64_t nth = (int64_t)gridDim.x * blockDim.x;
   for (int64_t e0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e0 < total; e0 += 4 * nth) {
@@ -412,6 +413,7 @@ __global__ void sppf_kernel(const float* __restrict__ x, float* __restrict__ y1,
 __global__ void sppf_image_kernel(const float* __restrict__ x, float* __restrict__ y1,
                                   float* __restrict__ y2, float* __restrict__ y3, Pool4 p, Pool4 q2,
                                   Pool4 q3, int cgroups) {
+  pdl_wait();
   extern __shared__ float sp_buf[];
   const int H = (int)p.h, W = (int)p.w, HW = H * W;
   float* a = sp_buf;                    // [H][W][SPPF_CG]
@@ -535,6 +537,7 @@ __global__ void upsample_nearest_nhwc4_kernel(const float* __restrict__ x, float
 // dimensions, where the source index is dst >> 1): each thread reads one input
 // float4 and writes the 2 x 2 output block; blockIdx.y walks input rows.
 __global__ void upsample2x_nhwc4_kernel(const float* __restrict__ x, float* __restrict__ y, Pool4 p) {
+  pdl_wait();
   const int c4 = (int)(p.c >> 2);
   const int row_elems = (int)p.w * c4;
   for (int64_t row = blockIdx.y; row < p.n * p.h; row += gridDim.y) {
@@ -627,6 +630,7 @@ __global__ void yolo_decode_kernel(DecodeArgs a) {
 // phase issues its float4 loads back to back so every line is fetched once.
 // The arithmetic is the generic kernel's, in the same order (same results).
 __global__ void __launch_bounds__(128) yolo_decode_rows_kernel(DecodeArgs a) {
+  pdl_wait();
   const int an = (int)(blockIdx.x * blockDim.x + threadIdx.x);
   if (an >= (int)a.anchors) return;
   int l = 0;
@@ -905,8 +909,9 @@ static int copy_impl(const mm_tensor_t* x_in, const mm_tensor_t* y_in, cudaStrea
     const int64_t cap = (int64_t)sm_count() * 16;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    copy_rows_vec4_kernel<<<(unsigned)blocks, 256, 0, s>>>(
-        (const float*)x->data, (float*)y->data, rows, (int)cols4, g[0].stride[0], g[1].stride[0]);
+    MM_CUDA(launch_pdl(copy_rows_vec4_kernel, dim3((unsigned)blocks), dim3(256), 0, s, (const float*)x->data,
+                       (float*)y->data, rows, (int)cols4, g[0].stride[0], g[1].stride[0]),
+            "mm_copy launch");
     MM_LAUNCH_CHECK("mm_copy launch");
     return MM_OK;
   }
@@ -1049,9 +1054,10 @@ extern "C" int mm_sppf_pool(const mm_tensor_t* x, const mm_tensor_t* y1, const m
     const int64_t blocks = p.n * cgroups;
     if (bytes <= 48 * 1024 && blocks > 0 && blocks <= 0x7fffffffLL) {
       cudaStream_t s = resolve_stream(stream);
-      sppf_image_kernel<<<(unsigned)blocks, 256, (size_t)bytes, s>>>(
-          (const float*)x->data, (float*)y1->data, (float*)y2->data, (float*)y3->data, p, q2, q3,
-          (int)cgroups);
+      MM_CUDA(launch_pdl(sppf_image_kernel, dim3((unsigned)blocks), dim3(256), (size_t)bytes, s,
+                         (const float*)x->data, (float*)y1->data, (float*)y2->data, (float*)y3->data, p,
+                         q2, q3, (int)cgroups),
+              "mm_sppf_pool launch");
       MM_LAUNCH_CHECK("mm_sppf_pool launch");
       return MM_OK;
     }
@@ -1163,7 +1169,9 @@ extern "C" int mm_upsample_nearest2d(const mm_tensor_t* x, double scale_h, doubl
     const int64_t row_elems = p.w * (p.c / 4);
     const dim3 grid((unsigned)std::min<int64_t>((row_elems + 255) / 256, 1024),
                     (unsigned)std::min<int64_t>(p.n * p.h, 65535));
-    upsample2x_nhwc4_kernel<<<grid, 256, 0, s>>>((const float*)x->data, (float*)y->data, p);
+    MM_CUDA(launch_pdl(upsample2x_nhwc4_kernel, grid, dim3(256), 0, s, (const float*)x->data,
+                       (float*)y->data, p),
+            "mm_upsample_nearest2d launch");
   } else if (nhwc4) {
     upsample_nearest_nhwc4_kernel<<<grid_for(total / 4, 256, (int64_t)sm_count() * 8), 256, 0, s>>>(
         (const float*)x->data, (float*)y->data, p, fh, fw);
@@ -1223,7 +1231,7 @@ extern "C" int mm_yolo_decode(const mm_tensor_t* const* feats, const float* stri
   }
   if (rows) {
     const dim3 grid((unsigned)((anchors + 127) / 128), (unsigned)std::min<int64_t>(a.batch, 65535));
-    yolo_decode_rows_kernel<<<grid, 128, 0, s>>>(a);
+    MM_CUDA(launch_pdl(yolo_decode_rows_kernel, grid, dim3(128), 0, s, a), "mm_yolo_decode launch");
     MM_LAUNCH_CHECK("mm_yolo_decode launch");
     return MM_OK;
   }
