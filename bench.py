@@ -49,6 +49,8 @@ def parse_args():
     p.add_argument("--e2e-chunks", type=int, default=4,
                    help="1 GPU: matrixman.infer chunks (upload / forward / readback overlap)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true",
+                   help="skip the output check against the CPU ground truth after the timed region")
     p.add_argument("--profile-case", action="store_true",
                    help="run --steps eager forwards (no graphs, no timing) for an ncu capture")
     p.add_argument("--profile-conv", default=None, metavar="C,K,KSIZE,STRIDE,HW",
@@ -177,6 +179,29 @@ def cpu_baseline(model, batch_sample: int, min_seconds: float = 12.0) -> dict:
                       f"fp32 ({cpu_model_name()}, {threads} threads), {el:.1f} s"}
 
 
+def output_parity(model, out_cpu, batch: int, world: int, images: int = 2) -> dict:
+    """Checker (outside every timed region): the first `images` images of each
+    rank's slice of the timed step's output against the CPU ground truth (the
+    unprepared model on torch CPU fp32, the same computation the CPU baseline
+    times), as max |diff| / max |ref| -- the parity bar is 1e-4."""
+    import torch
+    import workloads as W
+    from oracle.models import run_cpu
+    from oracle.tolerance import CONV_GEMM_REL, max_rel_err
+    worst = 0.0
+    for r in range(world):
+        x = W.yolo_input(batch, seed=1000 + r)[:images]
+        ref = run_cpu(model, x)
+        got = out_cpu[r * batch:r * batch + images]
+        worst = max(worst, max_rel_err(got, ref))
+        del x
+    return {"max_rel_err": worst, "bar": CONV_GEMM_REL, "ok": bool(worst < CONV_GEMM_REL),
+            "images_checked": images * world,
+            "what": f"first {images} images of each rank's slice of the last timed step's output"
+                    + (" (gathered on rank 0)" if world > 1 else "")
+                    + " vs the unprepared model on torch CPU fp32"}
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -252,6 +277,11 @@ def run_b200(args):
         launch_calls = profiling.total_launches() - launches0
         barrier()
         clock_info = clocks.stop()
+        # Parity of the last timed step's (gathered) output, checked after the
+        # timed region on rank 0.
+        parity = None
+        if rank == 0 and y is not None and not args.no_parity:
+            parity = output_parity(model, y.cpu(), batch, world)
         del y
     ms_step = ms_total / args.steps
     if world > 1:
@@ -295,6 +325,7 @@ def run_b200(args):
     return {"world": world, "rank": rank, "local": local, "value": value, "ms_step": ms_step,
             "clocks": clock_info, "e2e": e2e, "launch_calls": launch_calls, "prepared": prepared,
             "x_dev": x_dev, "model": model, "macs": macs_per_image(model), "batch": batch,
+            "parity": parity,
             "matrixman": matrixman, "dist": dist if world > 1 else None}
 
 
@@ -380,7 +411,7 @@ def main():
                    "batch_per_gpu": res["batch"], "global_batch": res["batch"] * res["world"],
                    "image": [IMAGE, IMAGE], "parallelism": f"replicas{res['world']}",
                    "l2": "inputs larger than L2 (315 MB input per step per GPU)"},
-        "e2e": res["e2e"], "roofline": roof,
+        "e2e": res["e2e"], "roofline": roof, "parity": res["parity"],
         "gpu_launches": kernels_per_forward * args.steps, "clocks": res["clocks"],
         "kernel_shares": shares,
     }

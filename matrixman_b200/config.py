@@ -21,8 +21,13 @@ B200 meaning of the north-star knobs:
 * ``activation_pool`` / ``scratch_pool`` -- ``safe``: released blocks are
   reusable immediately (ordering as above); ``deferred``: released blocks stay
   pending until their release event has completed.
-* ``tile_limit`` -- validated and reported; on CUDA it caps the number of output
-  rows per convolution launch chunk (``auto`` = no cap).
+* ``tile_limit`` -- validated, stored and reported with the reference's rules
+  (a positive integer or ``auto``), and locked after init like the other
+  runtime fields.  It has no effect on CUDA: the reference uses it to bound
+  the physical OpenGL texture tile a convolution renders into
+  (backends/opengl/convolution.py:1299-1320), a graphics-API size limit that
+  device buffers on B200 do not have, so every convolution runs as one
+  launch over its whole output.
 
 Settings without a CUDA meaning (OpenGL diagnostics) are accepted and
 reported so that existing scripts keep working; they have no effect.
@@ -50,7 +55,7 @@ _FIELDS: dict[str, tuple] = {
     "useDGPU": (False, "MATRIXMAN_USE_DGPU", "use_dgpu", "Backend / device", "backend-specific",
                 "Requests a discrete adapter (no effect on CUDA)."),
     "tileLimit": (256, "MATRIXMAN_TILE_LIMIT", "tile_limit", "OpenGL tiling", "stable",
-                  "Maximum tile dimension; on CUDA caps rows per conv launch chunk."),
+                  "Maximum OpenGL tile dimension (accepted and reported; no effect on CUDA)."),
     "tileSync": ("per_tile", "MATRIXMAN_TILE_SYNC", "tile_sync", "OpenGL tiling", "stable",
                  "Tiled-convolution synchronization (no effect on CUDA)."),
     "syncPolicy": ("safe", "MATRIXMAN_SYNC_POLICY", "sync_policy", "Synchronization", "stable",

@@ -6,10 +6,13 @@
 // Persistent CTAs (one per SM) walk a static list of 128-pixel x BN-channel
 // tiles (BN <= 80).  A k-block is 32 channels of one tap; a stage holds its A
 // tile (128 pixel rows x 128 B) and the B hi and B lo weight tiles (BN rows x
-// 128 B each, adjacent) in shared memory.  Warp roles:
+// 128 B each, adjacent) in shared memory.  The exact remainders of the A
+// tiles go to a separate, shorter ring of TMEM lo slots (32 columns each), so
+// the shared-memory pipeline is as deep as shared memory allows rather than
+// as TMEM allows.  Warp roles:
 //   * warps 0-7 (A producers, two per TMEM lane quarter): in the TMA modes
 //     they read their 32 rows x 16 channels of the A tile and write the exact
-//     remainder x - tf32(x) into a TMEM lo stage with tcgen05.st; in the
+//     remainder x - tf32(x) into a TMEM lo slot with tcgen05.st; in the
 //     gather mode they first fetch the tile with 16-byte cp.async (zero-fill
 //     for padding taps, rows past the end and padded channels);
 //   * warp 8 (TMA): prepacked [K_pad][R*S*C_pad] weight hi/lo planes, one 2-D
@@ -20,7 +23,7 @@
 //     from shared memory once for both products.  The [hi*hi | hi*lo] sums
 //     alternate between two period buffers handed over every `period` k-blocks;
 //   * warp 10 (lo MMAs): A lo (TMEM) times B hi, accumulated over a whole tile
-//     (~2^-11 of the result);
+//     (~2^-11 of the result); its commits free the stage and the lo slot;
 //   * warps 11-18 (accumulator, two per lane quarter): add each finished
 //     period's hi*hi + hi*lo into an fp32 total held in registers with
 //     round-to-nearest adds -- the tensor core's own accumulation rounds
@@ -296,7 +299,8 @@ struct TcArgs {
   int ntw, nth;   // TC_A_RECT: tiles across one output image
   int64_t mtiles; // pixel tiles
   int64_t tiles;  // mtiles * n_tiles
-  int stages;     // pipeline depth (A/B shared-memory stages == TMEM lo stages)
+  int stages;     // shared-memory pipeline depth (A + B hi + B lo stages)
+  int lo_slots;   // TMEM lo slots (2..TC_MAX_LO), a ring of its own
   int xbuf;       // lo*hi tile-sum buffers (2: the next tile's sum overlaps the epilogue)
   int epi_groups; // 2: two groups of 4 epilogue warps take alternate tiles (needs one hi*hi
                   // period per tile, xbuf == 2 and bn <= 48, so each group owns its buffers)
@@ -327,8 +331,9 @@ constexpr int TC_THREADS = (TC_WARP_EPI + TC_EPI_WARPS) * 32;
 constexpr uint32_t TC_TMEM_COLS = 512;
 constexpr int TC_LO_COLS = 32;     // TMEM columns per lo stage
 constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 4;  // one A tile: 128 rows x 128 B
-constexpr int TC_MAX_BN = 80;      // N tile limit (6 accumulator widths of bn columns + lo stages)
-constexpr int TC_MAX_STAGES = 8;
+constexpr int TC_MAX_BN = 80;      // N tile limit (5-6 accumulator widths of bn columns + lo slots)
+constexpr int TC_MAX_STAGES = 12;  // shared-memory stages (A + B hi + B lo)
+constexpr int TC_MAX_LO = 4;       // TMEM lo slots
 constexpr int TC_MAX_BIAS = 2048;  // output channels whose bias is staged in shared memory
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
@@ -426,10 +431,10 @@ struct TcSmem {
     l.bars = l.bias + (((uint32_t)kout * 4u + 15u) & ~15u);
     return l;
   }
-  // mbarriers: full_x[S], full_b[S], full_lo[S], empty[S], hh_full[2],
-  // hh_free[2], cross_full[2], cross_free[2], drain[3] (two used); then the
-  // TMEM slot.
-  __host__ __device__ int n_bars() const { return 4 * stages + 11; }
+  // mbarriers: full_x[S], full_b[S], fenced[S], empty[S], lo_full[TC_MAX_LO],
+  // lo_empty[TC_MAX_LO], hh_full[2], hh_free[2], cross_full[2],
+  // cross_free[2], drain[3] (two used); then the TMEM slot.
+  __host__ __device__ int n_bars() const { return 4 * stages + 2 * TC_MAX_LO + 11; }
   __host__ __device__ size_t bytes() const { return 1024 + bars + (size_t)n_bars() * 8 + 16; }
 };
 
@@ -504,35 +509,37 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int co
 // B hi and B lo tiles as one N = 2 bn operand, producing [hi*hi | hi*lo] in a
 // period buffer that the promotion warps fold into the fp32 total every
 // `period` k-blocks (two buffers alternate).  ROLE 1 (lo) reads the exact
-// remainder x - trunc(x) that the producer warps wrote into a TMEM lo stage
+// remainder x - trunc(x) that the producer warps wrote into a TMEM lo slot
 // and multiplies it by B hi into a per-tile buffer: its sum is ~2^-11 of the
 // result, so the tensor core's round-toward-zero accumulation leaves no
-// measurable drift there.  All 32 lanes run the loop and the waits (its state
-// stays warp-uniform); one elected lane issues.
+// measurable drift there.  Both issuers commit to the stage's `empty`
+// barrier; the lo issuer also frees the lo slot.  All 32 lanes run the loop
+// and the waits (its state stays warp-uniform); one elected lane issues.
+struct TcBars {
+  uint64_t *full_x, *full_b, *fenced, *empty, *lo_full, *lo_empty;
+  uint64_t *hh_full, *hh_free, *cross_full, *cross_free, *drain;
+};
+
 template <int ROLE>
 __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const TcSmem& L,
-                                         uint32_t tmem, uint64_t* full_x, uint64_t* full_b,
-                                         uint64_t* full_lo, uint64_t* empty, uint64_t* hh_full,
-                                         uint64_t* hh_free, uint64_t* cross_full,
-                                         uint64_t* cross_free, uint64_t* drain) {
-  const int S = a.stages, KB = a.kb_total;
+                                         uint32_t tmem, const TcBars& B) {
+  const int S = a.stages, KB = a.kb_total, LS = a.lo_slots;
   const int NP = (KB + a.period - 1) / a.period;
-  const uint32_t acc0 = (uint32_t)(TC_LO_COLS * S);
+  const uint32_t acc0 = (uint32_t)(TC_LO_COLS * LS);
   const uint32_t idesc = idesc_tf32(TC_BM, ROLE == 0 ? 2 * a.bn : a.bn);
-  // cp.async writes the gathered tile through the generic proxy: the hi MMAs
-  // then wait for full_lo, which every producer thread signals only after a
-  // proxy fence that makes its copies visible to the tensor core.
-  uint64_t* full_a = (ROLE == 1 || a.amode == TC_A_GATHER) ? full_lo : full_x;
+  const bool gather = a.amode == TC_A_GATHER;
   int64_t pc = 0, tc = 0;
   int st = 0;         // A/B stage of the next k-block
   uint32_t par = 0;   // its fill phase parity
+  int ls = 0;         // lo slot of the next k-block (ROLE 1)
+  uint32_t lpar = 0;  // its fill phase parity
   bool alive = true;
   for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x, ++tc) {
     const int xb = a.xbuf == 2 ? (int)(tc & 1) : 0;
     const uint32_t xpar = (uint32_t)((a.xbuf == 2 ? tc >> 1 : tc) & 1);
     uint32_t d = tmem + acc0 + (uint32_t)((4 + xb) * a.bn);
     if (ROLE == 1) {
-      if (!warp_wait(&cross_free[xb], xpar ^ 1u, TC_ERR_WAIT_ACC)) {
+      if (!warp_wait(&B.cross_free[xb], xpar ^ 1u, TC_ERR_WAIT_ACC)) {
         alive = false;
         break;
       }
@@ -541,7 +548,7 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
     for (int p = 0; p < NP && alive; ++p) {
       if (ROLE == 0) {
         const int b = (int)(pc & 1);
-        if (!warp_wait(&hh_free[b], (uint32_t)((pc >> 1) & 1) ^ 1u, TC_ERR_WAIT_ACC)) {
+        if (!warp_wait(&B.hh_free[b], (uint32_t)((pc >> 1) & 1) ^ 1u, TC_ERR_WAIT_ACC)) {
           alive = false;
           break;
         }
@@ -551,10 +558,17 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
       const int kb_begin = p * a.period;
       const int kb_end = min(KB, kb_begin + a.period);
       for (int kb = kb_begin; kb < kb_end; ++kb) {
-        // TMA modes: full_x carries the weights too (the lo issuer's full_lo
-        // follows the producers' wait on full_x).
-        if (!warp_wait(&full_a[st], par, TC_ERR_WAIT_A) ||
-            (a.amode == TC_A_GATHER && !warp_wait(&full_b[st], par, TC_ERR_WAIT_B))) {
+        // hi: the A tile in shared memory -- TMA modes: full_x (which carries
+        // the weights too); gather mode: `fenced`, which every producer thread
+        // signals after a proxy fence over its cp.async data, and full_b.
+        // lo: the lo slot (its producers waited for full_x first), and full_b
+        // in the gather mode.
+        bool ok;
+        if (ROLE == 0)
+          ok = warp_wait(gather ? &B.fenced[st] : &B.full_x[st], par, TC_ERR_WAIT_A);
+        else
+          ok = warp_wait(&B.lo_full[ls], lpar, TC_ERR_WAIT_A);
+        if (!ok || (gather && !warp_wait(&B.full_b[st], par, TC_ERR_WAIT_B))) {
           alive = false;
           break;
         }
@@ -567,32 +581,37 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
           for (int k = 0; k < TC_BK / 8; ++k) {
             const uint32_t acc = (first && k == 0) ? 0u : 1u;
             if (ROLE == 1)
-              mma_tf32_ts(d, tmem + (uint32_t)(st * TC_LO_COLS + 8 * k),
+              mma_tf32_ts(d, tmem + (uint32_t)(ls * TC_LO_COLS + 8 * k),
                           smem_desc_sw128(bs + 32 * k), idesc, acc);
             else
               mma_tf32(d, smem_desc_sw128(stage + 32 * k), smem_desc_sw128(bs + 32 * k), idesc, acc);
           }
-          mma_commit(&empty[st]);
+          mma_commit(&B.empty[st]);
+          if (ROLE == 1) mma_commit(&B.lo_empty[ls]);
         }
         if (++st == S) {
           st = 0;
           par ^= 1u;
         }
+        if (ROLE == 1 && ++ls == LS) {
+          ls = 0;
+          lpar ^= 1u;
+        }
       }
       if (ROLE == 0 && alive) {
-        if (elect_one()) mma_commit(&hh_full[pc & 1]);  // arrives once the period's MMAs complete
+        if (elect_one()) mma_commit(&B.hh_full[pc & 1]);  // arrives once the period's MMAs complete
         ++pc;
       }
     }
     if (ROLE == 1 && alive) {
-      if (elect_one()) mma_commit(&cross_full[xb]);
+      if (elect_one()) mma_commit(&B.cross_full[xb]);
     }
   }
   if (__any_sync(0xffffffffu, !alive || tc_error_raised())) {
     // Error path: no MMA of this warp may still write TMEM when it is freed.
-    if (elect_one()) mma_commit(&drain[ROLE]);
+    if (elect_one()) mma_commit(&B.drain[ROLE]);
     __syncwarp();
-    mbar_wait(&drain[ROLE], 0u, TC_ERR_WAIT_ACC);
+    mbar_wait(&B.drain[ROLE], 0u, TC_ERR_WAIT_ACC);
   }
 }
 
@@ -745,15 +764,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   float* bias_s = (float*)(smem + L.bias);
   const uint32_t b_bytes = (uint32_t)a.bn * 128;
   uint64_t* bars = (uint64_t*)(smem + L.bars);
-  uint64_t* full_x = bars;                // S: A tile (and, in the TMA modes, the B tiles)
-  uint64_t* full_b = bars + S;            // S: B tiles in the gather mode (TMA transaction bytes)
-  uint64_t* full_lo = bars + 2 * S;       // S: lo plane in TMEM (one arrival per producer thread)
-  uint64_t* empty = bars + 3 * S;         // S: one commit per issuer frees the stage
-  uint64_t* hh_full = bars + 4 * S;       // 2: [hi*hi | hi*lo] period complete in TMEM
-  uint64_t* hh_free = bars + 4 * S + 2;   // 2: one arrival per promotion thread
-  uint64_t* cross_full = bars + 4 * S + 4;  // 2: lo*hi tile sum complete
-  uint64_t* cross_free = bars + 4 * S + 6;  // 2: one arrival per epilogue thread
-  uint64_t* drain = bars + 4 * S + 8;       // 3: issuer error paths wait for their MMAs
+  TcBars B;
+  B.full_x = bars;                 // S: A tile (and, in the TMA modes, the B tiles)
+  B.full_b = bars + S;             // S: B tiles in the gather mode (TMA transaction bytes)
+  B.fenced = bars + 2 * S;         // S: gather mode, the A tile visible to the tensor core
+                                   //    (one arrival per producer thread, after a proxy fence)
+  B.empty = bars + 3 * S;          // S: one commit per issuer frees the stage
+  uint64_t* rest = bars + 4 * S;
+  B.lo_full = rest;                // LO: lo slot written (one arrival per producer thread)
+  B.lo_empty = rest + TC_MAX_LO;   // LO: the lo issuer's commit frees the slot
+  rest += 2 * TC_MAX_LO;
+  B.hh_full = rest;                // 2: [hi*hi | hi*lo] period complete in TMEM
+  B.hh_free = rest + 2;            // 2: one arrival per promotion thread
+  B.cross_full = rest + 4;         // 2: lo*hi tile sum complete
+  B.cross_free = rest + 6;         // 2: one arrival per epilogue thread
+  B.drain = rest + 8;              // 3: issuer error paths wait for their MMAs
+  uint64_t* full_x = B.full_x;
+  uint64_t* full_b = B.full_b;
+  uint64_t* empty = B.empty;
+  uint64_t* hh_full = B.hh_full;
+  uint64_t* hh_free = B.hh_free;
+  uint64_t* cross_full = B.cross_full;
+  uint64_t* cross_free = B.cross_free;
   uint32_t* tmem_slot = (uint32_t*)(bars + L.n_bars());
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -768,8 +800,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // (.noinc); TMA modes: the TMA thread's arrive + transaction bytes.
       mbar_init(&full_x[i], a.amode == TC_A_GATHER ? TC_A_WARPS * 32 : 1);
       mbar_init(&full_b[i], 1);
-      mbar_init(&full_lo[i], TC_A_WARPS * 32);
+      mbar_init(&B.fenced[i], TC_A_WARPS * 32);
       mbar_init(&empty[i], 2);
+    }
+    for (int i = 0; i < TC_MAX_LO; ++i) {
+      mbar_init(&B.lo_full[i], TC_A_WARPS * 32);
+      mbar_init(&B.lo_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&hh_full[i], 1);
@@ -779,7 +815,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&cross_full[i], 1);
       mbar_init(&cross_free[i], 32 * (a.epi_groups == 2 ? TC_EPI_WARPS / 2 : TC_EPI_WARPS));
     }
-    for (int i = 0; i < 3; ++i) mbar_init(&drain[i], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&B.drain[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == TC_WARP_HI) {
@@ -789,12 +825,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  for (int i = threadIdx.x; i < a.kout; i += TC_THREADS) bias_s[i] = a.bias ? a.bias[i] : 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Programmatic dependent launch: the set-up above (barriers, TMEM, bias, all
+  // Programmatic dependent launch: the set-up above (barriers, TMEM, both
   // independent of earlier kernels' results) overlaps the previous kernel's
   // tail; the next convolution may be scheduled from here on (its CTAs take an
   // SM only as one of ours leaves, one CTA per SM), and nothing below reads an
@@ -802,10 +837,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // Both instructions do nothing in a launch without the attribute.
   if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // TMEM columns: lo stages at [32 s, 32 s + 32); from acc0 = 32 S two period
+  // TMEM columns: lo slots at [32 l, 32 l + 32); from acc0 = 32 LO two period
   // buffers of 2 bn columns ([hi*hi | hi*lo], [acc0, acc0 + 4 bn)), then xbuf
   // lo*hi tile sums of bn columns.
-  const uint32_t acc0 = (uint32_t)(TC_LO_COLS * S);
+  const int LS = a.lo_slots;
+  const uint32_t acc0 = (uint32_t)(TC_LO_COLS * LS);
   const int KB = a.kb_total;
   const int NP = (KB + a.period - 1) / a.period;
   const int64_t my_tiles = a.tiles > blockIdx.x ? (a.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -821,6 +857,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t stage0 = smem_addr(smem);
     int st = 0;
     uint32_t par = 0;
+    int lo_slot = 0;     // lo slot of the k-block being split
+    uint32_t lo_par = 0;  // its fill phase parity
+    // Remainder of this warp's 32 rows x 16 channels of stage `st` into lo
+    // slot `lo_slot` once the lo issuer has freed it; false on a timeout.
+    auto split_into_slot = [&]() -> bool {
+      if (!mbar_wait(&B.lo_empty[lo_slot], lo_par ^ 1u, TC_ERR_WAIT_EMPTY)) return false;
+      tc_fence_after();
+      float lo[16];
+      const uint32_t tile_s = stage0 + (uint32_t)st * L.stage_bytes;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float4 v;
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                     : "r"(tile_s + sw128_off(q * 32 + lane, half * 4 + c4)));
+        lo[4 * c4 + 0] = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+        lo[4 * c4 + 1] = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+        lo[4 * c4 + 2] = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+        lo[4 * c4 + 3] = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+      }
+      tmem_st16(tm_rows + (uint32_t)(lo_slot * TC_LO_COLS + half * 16), lo);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(&B.lo_full[lo_slot]);
+      if (++lo_slot == LS) {
+        lo_slot = 0;
+        lo_par ^= 1u;
+      }
+      return true;
+    };
     if (a.amode == TC_A_GATHER) {
       // Gather: 16-byte cp.async of this warp's 32 rows x 64 B into the
       // swizzled A tile, zero-filled for padding taps, rows outside the output
@@ -905,24 +971,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         if (!alive) break;
         if (!mbar_wait(&full_x[st], par, TC_ERR_WAIT_A)) break;
+        // The gathered tile was written through the generic proxy: fence, then
+        // let the hi issuer read it.
         fence_proxy_async_smem();
-        float lo[16];
-        const uint32_t tile_s = stage0 + (uint32_t)st * L.stage_bytes;
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          float4 v;
-          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                       : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                       : "r"(tile_s + sw128_off(q * 32 + lane, half * 4 + c4)));
-          lo[4 * c4 + 0] = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-          lo[4 * c4 + 1] = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-          lo[4 * c4 + 2] = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-          lo[4 * c4 + 3] = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-        }
-        tmem_st16(tm_rows + (uint32_t)(st * TC_LO_COLS + half * 16), lo);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        tc_fence_before();
-        mbar_arrive(&full_lo[st]);
+        mbar_arrive(&B.fenced[st]);
+        if (!split_into_slot()) break;
         if (++st == S) {
           st = 0;
           par ^= 1u;
@@ -934,23 +987,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // TMA modes: the A tile arrives by TMA; only the remainder is computed.
       for (int64_t g = 0; g < total; ++g) {
         if (!mbar_wait(&full_x[st], par, TC_ERR_WAIT_A)) break;
-        float lo[16];
-        const uint32_t tile_s = stage0 + (uint32_t)st * L.stage_bytes;
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          float4 v;
-          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                       : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                       : "r"(tile_s + sw128_off(q * 32 + lane, half * 4 + c4)));
-          lo[4 * c4 + 0] = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-          lo[4 * c4 + 1] = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-          lo[4 * c4 + 2] = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-          lo[4 * c4 + 3] = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-        }
-        tmem_st16(tm_rows + (uint32_t)(st * TC_LO_COLS + half * 16), lo);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        tc_fence_before();
-        mbar_arrive(&full_lo[st]);
+        if (!split_into_slot()) break;
         if (++st == S) {
           st = 0;
           par ^= 1u;
@@ -1016,11 +1053,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else if (warp == TC_WARP_HI) {
-    tc_issue<0>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
-                cross_free, drain);
+    tc_issue<0>(a, smem, L, tmem, B);
   } else if (warp == TC_WARP_LO) {
-    tc_issue<1>(a, smem, L, tmem, full_x, full_b, full_lo, empty, hh_full, hh_free, cross_full,
-                cross_free, drain);
+    tc_issue<1>(a, smem, L, tmem, B);
   } else if (warp >= TC_WARP_EPI) {
     // ---------------- promotion (fp32 RN adds) + epilogue ----------------
     // Two warps per TMEM lane quarter; warp half h owns the 16-column chunks
@@ -1039,6 +1074,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const int nchunk = a.bn >> 4;
     uint8_t* stg = smem + L.stg + (size_t)(warp - TC_WARP_EPI) * a.stg_chunks * TC_STG_BOX;
+    // The bias may be the output of an earlier kernel in the stream, so it is
+    // staged only after griddepcontrol.wait, by the epilogue warps that read
+    // it (named barrier 1 over their 256 threads).
+    for (int i = threadIdx.x - TC_WARP_EPI * 32; i < a.kout; i += TC_EPI_WARPS * 32)
+      bias_s[i] = a.bias ? a.bias[i] : 0.f;
+    asm volatile("bar.sync 1, %0;" ::"n"(TC_EPI_WARPS * 32) : "memory");
     int64_t tc = grp ? eg : 0;
     bool alive = true;
     for (int64_t tile = blockIdx.x + tc * gridDim.x; tile < a.tiles && alive;
@@ -1472,16 +1513,35 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   // Staging per epilogue warp: its chunks of one tile (all of them when the
   // two-group epilogue may be chosen, bn <= 48; half of them otherwise).
   const int stg_bound = staged ? (a.bn <= 16 * TC_EPI_CHUNKS ? nchunk : (nchunk + 1) / 2) : 0;
-  // Two cross-term sets when at least 4 stages still fit, else one.
+  // TMEM: lo slots of 32 columns, two [hi*hi | hi*lo] period buffers of 2 bn
+  // columns and xbuf lo*hi tile sums of bn columns.  Two tile sums (the next
+  // tile's sum overlaps the epilogue) when at least two lo slots still fit,
+  // else one; as many lo slots as fit, up to TC_MAX_LO.  Shared memory: as
+  // many A + B stages as fit (the lo ring no longer bounds them).
+  a.xbuf = 0;
+  for (int xbuf = 2; xbuf >= 1 && a.xbuf == 0; --xbuf) {
+    const int free_cols = (int)TC_TMEM_COLS - (4 + xbuf) * a.bn;
+    const int slots = free_cols / TC_LO_COLS;
+    if (slots >= 2) {
+      a.xbuf = xbuf;
+      a.lo_slots = slots < TC_MAX_LO ? slots : TC_MAX_LO;
+    }
+  }
+  if (a.xbuf == 0) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: N tile too wide");
+  if (const char* lo_env = std::getenv("MATRIXMAN_TC_LO_SLOTS")) {
+    const int v = std::atoi(lo_env);
+    if (v >= 2 && v <= a.lo_slots) a.lo_slots = v;
+  }
+  int max_stages = TC_MAX_STAGES;
+  if (const char* st_env = std::getenv("MATRIXMAN_TC_STAGES")) {
+    const int v = std::atoi(st_env);
+    if (v >= 2 && v <= TC_MAX_STAGES) max_stages = v;
+  }
   int stages = 0;
-  for (int xbuf = 2; xbuf >= 1 && stages == 0; --xbuf) {
-    for (int st = TC_MAX_STAGES; st >= (xbuf == 2 ? 4 : 3); --st) {
-      if (TC_LO_COLS * st + (4 + xbuf) * a.bn <= (int)TC_TMEM_COLS &&
-          TcSmem::make(a.bn, st, k_out, stg_bound).bytes() <= smem_limit) {
-        stages = st;
-        a.xbuf = xbuf;
-        break;
-      }
+  for (int st = max_stages; st >= 2; --st) {
+    if (TcSmem::make(a.bn, st, k_out, stg_bound).bytes() <= smem_limit) {
+      stages = st;
+      break;
     }
   }
   if (stages == 0) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: N tile too wide");

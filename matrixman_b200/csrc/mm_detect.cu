@@ -27,6 +27,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -88,6 +89,16 @@ struct DetWork {
 };
 
 __host__ __device__ inline size_t det_align(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Largest batch * anchors the workspace arithmetic accepts: 2^40 anchors in
+// all (16 TiB of boxes) keeps every size below 2^48 bytes, far from size_t
+// overflow, and above any real detection batch.
+constexpr int64_t DET_MAX_BATCH_ANCHORS = (int64_t)1 << 40;
+
+inline bool det_sizes_ok(int64_t batch, int64_t anchors) {
+  return batch >= 0 && anchors >= 0 && batch <= 0x7fffffffLL && anchors <= 0x7fffffffLL &&
+         (batch == 0 || anchors <= DET_MAX_BATCH_ANCHORS / batch);
+}
 
 // Byte offsets of the workspace parts (DetWork order); returns the total size.
 __host__ __device__ inline size_t det_work_layout(int64_t batch, int64_t anchors, size_t off[6]) {
@@ -324,6 +335,8 @@ extern "C" int mm_detect_reduce(const mm_tensor_t* pred, const mm_tensor_t* out,
 extern "C" int mm_detect_nms_workspace_size(int64_t batch, int64_t anchors, size_t* bytes) {
   if (bytes == nullptr || batch < 0 || anchors < 0)
     return fail(MM_ERR_INVALID, "mm_detect_nms_workspace_size: bad arguments");
+  if (!det_sizes_ok(batch, anchors))
+    return fail(MM_ERR_UNSUPPORTED, "mm_detect_nms_workspace_size: batch x anchors too large");
   size_t off[6];
   *bytes = det_work_layout(batch, anchors, off);
   return MM_OK;
@@ -341,7 +354,7 @@ extern "C" int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_
       dets->size[2] != 6)
     return fail(MM_ERR_INVALID, "mm_detect_nms: detections must be [B, max_det, 6]");
   if (counts == nullptr && pred->size[0] > 0) return fail(MM_ERR_INVALID, "mm_detect_nms: null counts");
-  if (pred->size[1] - 4 > 32767 || pred->size[0] > 0x7fffffffLL || pred->size[2] > 0x7fffffffLL)
+  if (pred->size[1] - 4 > 32767 || !det_sizes_ok(pred->size[0], pred->size[2]))
     return fail(MM_ERR_UNSUPPORTED, "mm_detect_nms: too many classes, images or anchors");
   if (pred->size[0] == 0) return MM_OK;
   size_t off[6];
@@ -373,14 +386,16 @@ extern "C" int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_
   w.keep = (int*)(base + off[4]);
   w.count = (int*)(base + off[5]);
   {
-    static bool configured[256] = {};
+    // Once per device; host threads may race here, which only repeats the
+    // (idempotent) attribute call.
+    static std::atomic<bool> configured[256];
     int dev = 0;
     MM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-    if (dev >= 0 && dev < 256 && !configured[dev]) {
+    if (dev >= 0 && dev < 256 && !configured[dev].load(std::memory_order_acquire)) {
       MM_CUDA(cudaFuncSetAttribute(detect_nms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)DET_SMEM),
               "mm_detect_nms: shared memory attribute");
-      configured[dev] = true;
+      configured[dev].store(true, std::memory_order_release);
     }
   }
   cudaStream_t s = resolve_stream(stream);
@@ -405,7 +420,30 @@ static __device__ __align__(256) uint8_t det_static_work[MM_DETECT_STATIC_WORK_B
 
 namespace {
 std::mutex det_static_mu;
-void* det_static_addr[256] = {};  // device address of det_static_work, per device
+// Device address of det_static_work per device, with the context it was
+// looked up in: a device reset (cudaDeviceReset) makes a new context in
+// which the module, and so the array, is loaded again at another address.
+void* det_static_addr[256] = {};
+void* det_static_ctx[256] = {};
+
+// The calling thread's current CUDA context (cuCtxGetCurrent through the
+// runtime's driver entry point, so the library does not link libcuda).
+int current_context(void** ctx) {
+  using GetCtxFn = int (*)(void**);
+  static GetCtxFn get_ctx = nullptr;
+  if (get_ctx == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        fn == nullptr || q != cudaDriverEntryPointSuccess)
+      return fail(MM_ERR_CUDA, "mm_detect_nms_static: cuCtxGetCurrent entry point unavailable");
+    get_ctx = (GetCtxFn)fn;
+  }
+  *ctx = nullptr;
+  if (get_ctx(ctx) != 0 || *ctx == nullptr)
+    return fail(MM_ERR_STATE, "mm_detect_nms_static: no current CUDA context");
+  return MM_OK;
+}
 }  // namespace
 
 extern "C" int mm_detect_nms_static(const mm_tensor_t* pred, float conf_thr, float iou_thr,
@@ -414,6 +452,8 @@ extern "C" int mm_detect_nms_static(const mm_tensor_t* pred, float conf_thr, flo
   int rc;
   if ((rc = validate(pred, "mm_detect_nms_static prediction", MM_F32)) != MM_OK) return rc;
   if (pred->ndim == 3 && pred->size[0] > 0) {
+    if (!det_sizes_ok(pred->size[0], pred->size[2]))
+      return fail(MM_ERR_UNSUPPORTED, "mm_detect_nms_static: too many images or anchors");
     size_t off[6];
     const size_t need = det_work_layout(pred->size[0], pred->size[2], off);
     if (need > (size_t)MM_DETECT_STATIC_WORK_BYTES)
@@ -427,15 +467,21 @@ extern "C" int mm_detect_nms_static(const mm_tensor_t* pred, float conf_thr, flo
   int dev = 0;
   MM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev < 0 || dev >= 256) return fail(MM_ERR_UNSUPPORTED, "mm_detect_nms_static: device index above 255");
+  // The first call on a device (with that device current) makes sure the
+  // runtime's context exists (cudaSetDevice initialises it), then looks up
+  // the array's device address in it (the name itself is only a host-side
+  // stand-in); later calls reuse the address while that context lives.
+  MM_CUDA(cudaSetDevice(dev), "mm_detect_nms_static: context");
+  void* ctx = nullptr;
+  if ((rc = current_context(&ctx)) != MM_OK) return rc;
   void* work = nullptr;
   {
-    // First call on a device: the array's device address (the name itself is
-    // only a host-side stand-in).
     std::lock_guard<std::mutex> lock(det_static_mu);
-    if (det_static_addr[dev] == nullptr) {
+    if (det_static_addr[dev] == nullptr || det_static_ctx[dev] != ctx) {
       void* addr = nullptr;
       MM_CUDA(cudaGetSymbolAddress(&addr, det_static_work), "mm_detect_nms_static: static scratch address");
       det_static_addr[dev] = addr;
+      det_static_ctx[dev] = ctx;
     }
     work = det_static_addr[dev];
   }

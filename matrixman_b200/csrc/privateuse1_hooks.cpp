@@ -34,6 +34,10 @@ F resolve(const char* name) {
 
 thread_local int t_current_device = 0;
 
+// Upper bound of every stream wait the guard makes (matrixman.config
+// waitTimeoutMs, passed in at backend init; the config is locked from then on).
+std::atomic<int64_t> g_wait_timeout_ms{600000};
+
 int device_count() {
   int n = 0;
   if (resolve<count_fn>("mm_device_count")(&n) != 0) return 0;
@@ -45,6 +49,21 @@ void* runtime_stream(int device) {
   resolve<dev_fn>("mm_init")(device);
   resolve<stream_fn>("mm_runtime_stream")(device, &s);
   return s;
+}
+
+constexpr int MM_STATUS_TIMEOUT = 5;  // MM_ERR_TIMEOUT of the C ABI
+
+// Bounded synchronisation of a device's runtime stream: raises with the C
+// ABI's message when the wait gives up (MM_ERR_TIMEOUT) or fails.
+void sync_runtime_stream(int device, const char* what) {
+  const int rc = resolve<sync_fn>("mm_stream_sync")(runtime_stream(device), g_wait_timeout_ms.load());
+  if (rc == 0) return;
+  char msg[512] = {0};
+  using err_fn = int (*)(char*, size_t);
+  if (void* p = dlsym(RTLD_DEFAULT, "mm_last_error")) reinterpret_cast<err_fn>(p)(msg, sizeof(msg));
+  TORCH_CHECK(rc != MM_STATUS_TIMEOUT, "matrixman guard: ", what, " of device ", device,
+              " did not finish within ", g_wait_timeout_ms.load(), " ms (waitTimeoutMs): ", msg);
+  TORCH_CHECK(false, "matrixman guard: ", what, " of device ", device, " failed: ", msg);
 }
 
 using pin_alloc_fn = int (*)(size_t, void**);
@@ -143,13 +162,11 @@ class MatrixManGuardImpl final : public c10::impl::DeviceGuardImplInterface {
   }
 
   void synchronizeStream(const c10::Stream& s) const override {
-    TORCH_CHECK(resolve<sync_fn>("mm_stream_sync")(runtime_stream(s.device_index()), -1) == 0,
-                "matrixman guard: stream synchronize failed");
+    sync_runtime_stream(s.device_index(), "stream synchronize");
   }
 
   void synchronizeDevice(const c10::DeviceIndex idx) const override {
-    TORCH_CHECK(resolve<sync_fn>("mm_stream_sync")(runtime_stream(idx), -1) == 0,
-                "matrixman guard: device synchronize failed");
+    sync_runtime_stream(idx, "device synchronize");
   }
 };
 
@@ -167,9 +184,18 @@ void register_hooks() {
 
 int guard_device_count() { return (int)MatrixManGuardImpl().deviceCount(); }
 
+void set_wait_timeout_ms(int64_t ms) {
+  TORCH_CHECK(ms > 0, "matrixman hooks: wait timeout must be positive");
+  g_wait_timeout_ms.store(ms);
+}
+
+int64_t wait_timeout_ms() { return g_wait_timeout_ms.load(); }
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("register_hooks", &register_hooks, "Register the matrixman PrivateUse1 hooks");
   m.def("device_count", &guard_device_count, "Device count seen by the DeviceGuard");
+  m.def("set_wait_timeout_ms", &set_wait_timeout_ms, "Bound of the guard's stream waits (ms)");
+  m.def("wait_timeout_ms", &wait_timeout_ms, "Bound of the guard's stream waits (ms)");
 }

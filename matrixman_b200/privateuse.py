@@ -109,5 +109,8 @@ def register_native_hooks() -> bool:
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
     module.register_hooks()
+    # The guard's stream waits are bounded like every other host wait.
+    from .config import config
+    module.set_wait_timeout_ms(int(config.waitTimeoutMs))
     _native = module
     return True

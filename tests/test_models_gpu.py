@@ -55,6 +55,47 @@ def test_yolov8n_prepared(mm, batch):
     assert rep.folded == 57 and rep.detection_head_prepared == 1
 
 
+def test_yolov8n_prepared_bs64(mm):
+    """The benchmark's own configuration: YOLOv8n 640x640 at 64 images, eager
+    forward, graph capture and graph replay, each against the CPU oracle."""
+    model = W.yolov8_model("n")
+    x = W.yolo_input(64, seed=1000)
+    _check(mm, model, x, calls=3)
+
+
+def test_yolov8m_prepared_bs8(mm):
+    """A batch-8 slice of the YOLOv8m bs256 configuration (eager + graph)."""
+    model = W.yolov8_model("m")
+    x = W.yolo_input(8, seed=7)
+    _check(mm, model, x, calls=2)
+
+
+def test_parameter_cache_reuploads_after_inplace_edit(mm):
+    """An in-place edit of a CPU weight bumps its version, and the next eager
+    call uploads it again (reference backends/cuda/backend.py:241-294); an
+    unchanged weight is served from the cache."""
+    from matrixman_b200 import runtime
+    g = torch.Generator().manual_seed(11)
+    conv = torch.nn.Conv2d(8, 16, 3, padding=1, bias=True).eval()
+    x = torch.rand(2, 8, 24, 24, generator=g) * 2 - 1
+    rt = runtime.get_runtime(runtime.current_device())
+    with torch.no_grad():
+        xd = mm.to_device(x)
+        y1 = conv(xd).cpu()
+        size1 = rt.parameter_cache_size()
+        y1b = conv(xd).cpu()
+        assert rt.parameter_cache_size() == size1
+        assert torch.equal(y1, y1b)
+        conv.weight.mul_(-2.0)
+        conv.bias.add_(0.5)
+        y2 = conv(xd).cpu()
+        ref2 = conv(x)
+    assert max_rel_err(y1, torch.nn.functional.conv2d(x, conv.weight / -2.0, conv.bias - 0.5,
+                                                      padding=1)) < CONV_GEMM_REL
+    assert max_rel_err(y2, ref2) < CONV_GEMM_REL
+    assert not torch.allclose(y1, y2)
+
+
 def test_yolov8n_unprepared_eager(mm):
     model = W.yolov8_model("n")
     x = W.yolo_input(1, size=320)
