@@ -4,27 +4,34 @@
 // (tap r, tap s, channel c) with channels padded to C_pad (multiple of 32).
 //
 // Persistent CTAs (one per SM) walk a static list of 128-pixel x BN-channel
-// tiles (BN <= 80).  A k-block is 32 channels of one tap; a stage holds its A
-// tile (128 pixel rows x 128 B) and the B hi and B lo weight tiles (BN rows x
-// 128 B each, adjacent) in shared memory.  The exact remainders of the A
-// tiles go to a separate, shorter ring of TMEM lo slots (32 columns each), so
-// the shared-memory pipeline is as deep as shared memory allows rather than
-// as TMEM allows.  Warp roles:
-//   * warps 0-7 (A producers, two per TMEM lane quarter): in the TMA modes
-//     they read their 32 rows x 16 channels of the A tile and write the exact
+// tiles (BN <= 80).  A sub-block is 32 channels of one tap; a k-block is
+// KSUB (1 or 2, a template parameter) consecutive sub-blocks, the unit that
+// every warp role hands on -- each k-block costs every role a fixed chain of
+// barrier waits, copies and MMA issues, so deep reductions run two
+// sub-blocks per k-block.  A stage holds the k-block's A tiles (128 pixel rows
+// x 128 B each) and, per sub-block, the adjacent B hi and B lo weight tiles
+// (BN rows x 128 B each) in shared memory.  The exact remainders of the A
+// tiles go to a separate, shorter ring of TMEM lo slots (32 columns per
+// sub-block), so the shared-memory pipeline is as deep as shared memory
+// allows rather than as TMEM allows.  Warp roles (15 warps, at most four per
+// SM sub-partition, so 128 registers per thread):
+//   * warps 0-3 (A producers, one per TMEM lane quarter): in the TMA modes
+//     they read their 32 rows x 32 channels of each A tile and write the exact
 //     remainder x - tf32(x) into a TMEM lo slot with tcgen05.st; in the
-//     gather mode they first fetch the tile with 16-byte cp.async (zero-fill
+//     gather mode they first fetch the tiles with 16-byte cp.async (zero-fill
 //     for padding taps, rows past the end and padded channels);
-//   * warp 8 (TMA): prepacked [K_pad][R*S*C_pad] weight hi/lo planes, one 2-D
-//     tiled load each per stage, and the A tile in the TMA modes;
-//   * warp 9 (hi MMAs): A (fp32 in shared memory, which the tensor core reads
+//   * warp 4 (TMA): prepacked [K_pad][R*S*C_pad] weight hi/lo planes, one 2-D
+//     tiled load each per sub-block, and the A tiles in the TMA modes;
+//   * warp 5 (hi MMAs): A (fp32 in shared memory, which the tensor core reads
 //     as tf32 -- the high part of the split) times [B hi | B lo] as one
 //     N = 2 BN tcgen05.mma.kind::tf32 per 8 channels, so each A slice is read
 //     from shared memory once for both products.  The [hi*hi | hi*lo] sums
 //     alternate between two period buffers handed over every `period` k-blocks;
-//   * warp 10 (lo MMAs): A lo (TMEM) times B hi, accumulated over a whole tile
-//     (~2^-11 of the result); its commits free the stage and the lo slot;
-//   * warps 11-18 (accumulator, two per lane quarter): add each finished
+//   * warp 6 (lo MMAs): A lo (TMEM) times B hi, accumulated over a whole tile
+//     (~2^-11 of the result); its commits free the stage and the lo slot.
+//     Two issuing warps: tcgen05.mma issue from one thread takes about as
+//     long as MMAs of these shapes run;
+//   * warps 7-14 (accumulator, two per lane quarter): add each finished
 //     period's hi*hi + hi*lo into an fp32 total held in registers with
 //     round-to-nearest adds -- the tensor core's own accumulation rounds
 //     toward zero, so long reductions inside TMEM drift by ~K * 2^-24 -- then
@@ -184,6 +191,17 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   return d;
 }
 
+// The same descriptor split into its halves: the high word is a constant
+// (stride byte offset, version, swizzle mode); the low word holds the start
+// address and the leading byte offset, so stepping along K (32 bytes) adds 2.
+constexpr uint32_t TC_DESC_HI = (uint32_t)(1024 >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t smem_desc_lo(uint32_t addr) {
+  return ((addr >> 4) & 0x3FFFu) | (1u << 16);
+}
+__device__ __forceinline__ uint64_t desc_of(uint32_t lo) {
+  return ((uint64_t)TC_DESC_HI << 32) | lo;
+}
+
 // Instruction descriptor for kind::tf32, fp32 accumulate, K-major A and B.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
   return (1u << 4)                      // D format: f32
@@ -290,7 +308,9 @@ struct TcArgs {
   int oh, ow, kout;
   int r, s, sh, sw, ph, pw, dh, dw;
   int m_total;    // output pixels (fits in 31 bits; checked on the host)
-  int kb_total;   // r * s * (c_pad / 32)
+  int sb_total;   // 32-channel sub-blocks of the reduction: r * s * (c_pad / 32)
+  int ksub;       // sub-blocks per k-block (1 or 2; a template parameter of the kernel)
+  int kb_total;   // k-blocks per tile: ceil(sb_total / ksub)
   int cb;         // c_pad / 32
   int bn;         // N tile: multiple of 16, <= TC_MAX_BN
   int n_tiles;    // ceil(kout / bn)
@@ -300,7 +320,7 @@ struct TcArgs {
   int64_t mtiles; // pixel tiles
   int64_t tiles;  // mtiles * n_tiles
   int stages;     // shared-memory pipeline depth (A + B hi + B lo stages)
-  int lo_slots;   // TMEM lo slots (2..TC_MAX_LO), a ring of its own
+  int lo_slots;   // TMEM lo slots (2..TC_MAX_LO, ksub * 32 columns each), a ring of its own
   int xbuf;       // lo*hi tile-sum buffers (2: the next tile's sum overlaps the epilogue)
   int epi_groups; // 2: two groups of 4 epilogue warps take alternate tiles (needs one hi*hi
                   // period per tile, xbuf == 2 and bn <= 48, so each group owns its buffers)
@@ -320,16 +340,19 @@ constexpr int TC_A_RECT = 2;    // one 4-D TMA load of a th x tw output-pixel re
                                 // (conv strides become TMA traversal strides)
 
 // Warp roles of the persistent kernel.
-constexpr int TC_A_WARPS = 8;      // warps 0-7: A producers (2 per TMEM lane quarter)
-constexpr int TC_WARP_TMA = 8;     // warp 8: TMA (weights; A in the TMA modes)
-constexpr int TC_WARP_HI = 9;      // warp 9: A hi * [B hi | B lo] MMA issue + TMEM owner
-constexpr int TC_WARP_LO = 10;     // warp 10: A lo * B hi MMA issue
-constexpr int TC_WARP_EPI = 11;    // warps 11-18: promotion + epilogue (2 per lane quarter)
+// 15 warps: with at most four warps per SM sub-partition each thread may hold
+// 128 registers (the epilogue keeps a tile row's fp32 total in registers).
+constexpr int TC_A_WARPS = 4;      // warps 0-3: A producers (one per TMEM lane quarter)
+constexpr int TC_A_HALVES = 8 / TC_A_WARPS;  // 16-channel halves of a sub-block per producer warp
+constexpr int TC_WARP_TMA = TC_A_WARPS;       // TMA (weights; A in the TMA modes)
+constexpr int TC_WARP_HI = TC_A_WARPS + 1;    // A hi * [B hi | B lo] MMA issue + TMEM owner
+constexpr int TC_WARP_LO = TC_A_WARPS + 2;    // A lo * B hi MMA issue
+constexpr int TC_WARP_EPI = TC_A_WARPS + 3;   // 8 warps: promotion + epilogue (2 per lane quarter)
 constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_EPI_CHUNKS = 3;   // 16-column chunks per epilogue warp (bn <= 96)
 constexpr int TC_THREADS = (TC_WARP_EPI + TC_EPI_WARPS) * 32;
 constexpr uint32_t TC_TMEM_COLS = 512;
-constexpr int TC_LO_COLS = 32;     // TMEM columns per lo stage
+constexpr int TC_LO_COLS = 32;     // TMEM columns per sub-block in a lo slot
 constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 4;  // one A tile: 128 rows x 128 B
 constexpr int TC_MAX_BN = 80;      // N tile limit (5-6 accumulator widths of bn columns + lo slots)
 constexpr int TC_MAX_STAGES = 12;  // shared-memory stages (A + B hi + B lo)
@@ -416,16 +439,18 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 constexpr uint32_t TC_STG_BOX = 32 * 64;
 
 // Shared-memory layout of one CTA (offsets from the 1024-aligned base).  A
-// stage holds the A tile (128 pixel rows x 128 B, 128-byte swizzle) and the B
-// hi and lo tiles (bn rows x 128 B each); every stage offset is a multiple of
-// 1024 bytes, as the swizzled layout requires.
+// stage holds the ksub A tiles of a k-block (128 pixel rows x 128 B each,
+// 128-byte swizzle), then per sub-block the adjacent B hi and lo tiles (bn
+// rows x 128 B each); every tile offset is a multiple of 1024 bytes, as the
+// swizzled layout requires.
 struct TcSmem {
-  uint32_t stage_bytes, stg, bias, bars;
+  uint32_t a_bytes, stage_bytes, stg, bias, bars;
   int stages;
-  __host__ __device__ static TcSmem make(int bn, int stages, int kout, int stg_chunks) {
+  __host__ __device__ static TcSmem make(int bn, int ksub, int stages, int kout, int stg_chunks) {
     TcSmem l;
     l.stages = stages;
-    l.stage_bytes = TC_A_BYTES + 2u * (uint32_t)bn * 128u;
+    l.a_bytes = (uint32_t)ksub * TC_A_BYTES;
+    l.stage_bytes = l.a_bytes + (uint32_t)ksub * 2u * (uint32_t)bn * 128u;
     l.stg = (uint32_t)stages * l.stage_bytes;           // epilogue staging (1024-aligned)
     l.bias = l.stg + (uint32_t)TC_EPI_WARPS * (uint32_t)stg_chunks * TC_STG_BOX;  // kout floats, 16-byte padded
     l.bars = l.bias + (((uint32_t)kout * 4u + 15u) & ~15u);
@@ -520,12 +545,14 @@ struct TcBars {
   uint64_t *hh_full, *hh_free, *cross_full, *cross_free, *drain;
 };
 
-template <int ROLE>
+template <int ROLE, int KS>
 __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const TcSmem& L,
                                          uint32_t tmem, const TcBars& B) {
   const int S = a.stages, KB = a.kb_total, LS = a.lo_slots;
   const int NP = (KB + a.period - 1) / a.period;
-  const uint32_t acc0 = (uint32_t)(TC_LO_COLS * LS);
+  const uint32_t slot_cols = (uint32_t)(TC_LO_COLS * KS);
+  const uint32_t acc0 = slot_cols * (uint32_t)LS;
+  const uint32_t bpair = 2u * (uint32_t)a.bn * 128u;  // one sub-block's B hi + B lo bytes
   const uint32_t idesc = idesc_tf32(TC_BM, ROLE == 0 ? 2 * a.bn : a.bn);
   const bool gather = a.amode == TC_A_GATHER;
   int64_t pc = 0, tc = 0;
@@ -574,17 +601,28 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
         }
         tc_fence_after();
         const uint32_t stage = smem_addr(smem + (size_t)st * L.stage_bytes);
-        const uint32_t bs = stage + TC_A_BYTES;  // B hi, then B lo (bn rows each)
         const bool first = ROLE == 0 ? kb == kb_begin : kb == 0;
+        const int nsub = min(KS, a.sb_total - kb * KS);
         if (elect_one()) {
+          const uint32_t b_lo0 = smem_desc_lo(stage + L.a_bytes);  // B hi, then B lo (bn rows each)
+          const uint32_t a_lo0 = smem_desc_lo(stage);
+          const uint32_t lo_col = tmem + (uint32_t)ls * slot_cols;
 #pragma unroll
-          for (int k = 0; k < TC_BK / 8; ++k) {
-            const uint32_t acc = (first && k == 0) ? 0u : 1u;
-            if (ROLE == 1)
-              mma_tf32_ts(d, tmem + (uint32_t)(ls * TC_LO_COLS + 8 * k),
-                          smem_desc_sw128(bs + 32 * k), idesc, acc);
-            else
-              mma_tf32(d, smem_desc_sw128(stage + 32 * k), smem_desc_sw128(bs + 32 * k), idesc, acc);
+          for (int j = 0; j < KS; ++j) {
+            if (j < nsub) {
+              // (one A tile is 16 KB = 1024 descriptor units; a B pair 2 bn x 128 B)
+              const uint32_t bd = b_lo0 + (uint32_t)j * (bpair >> 4);
+              const uint32_t ad = a_lo0 + (uint32_t)j * (TC_A_BYTES >> 4);
+#pragma unroll
+              for (int k = 0; k < TC_BK / 8; ++k) {
+                const uint32_t acc = (first && j == 0 && k == 0) ? 0u : 1u;
+                if (ROLE == 1)
+                  mma_tf32_ts(d, lo_col + (uint32_t)(j * TC_LO_COLS + 8 * k), desc_of(bd + 2 * k), idesc,
+                              acc);
+                else
+                  mma_tf32(d, desc_of(ad + 2 * k), desc_of(bd + 2 * k), idesc, acc);
+              }
+            }
           }
           mma_commit(&B.empty[st]);
           if (ROLE == 1) mma_commit(&B.lo_empty[ls]);
@@ -751,7 +789,7 @@ __device__ __forceinline__ void tc_stage_row(const TcArgs& a, float (&tot)[TC_EP
 // One instantiation per activation and residual mode (RM 0 none, 1 added
 // before the activation, 2 after): each carries a single epilogue, which keeps
 // the code that the producer, TMA and MMA warps run beside it small.
-template <int ACT, int RM>
+template <int ACT, int RM, int KS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap_hi,
                    const __grid_constant__ CUtensorMap wmap_lo,
@@ -760,7 +798,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int S = a.stages;
-  const TcSmem L = TcSmem::make(a.bn, S, a.kout, a.stg_chunks);
+  const TcSmem L = TcSmem::make(a.bn, KS, S, a.kout, a.stg_chunks);
   float* bias_s = (float*)(smem + L.bias);
   const uint32_t b_bytes = (uint32_t)a.bn * 128;
   uint64_t* bars = (uint64_t*)(smem + L.bars);
@@ -841,7 +879,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // buffers of 2 bn columns ([hi*hi | hi*lo], [acc0, acc0 + 4 bn)), then xbuf
   // lo*hi tile sums of bn columns.
   const int LS = a.lo_slots;
-  const uint32_t acc0 = (uint32_t)(TC_LO_COLS * LS);
+  const uint32_t slot_cols = (uint32_t)(TC_LO_COLS * KS);
+  const uint32_t acc0 = slot_cols * (uint32_t)LS;
   const int KB = a.kb_total;
   const int NP = (KB + a.period - 1) / a.period;
   const int64_t my_tiles = a.tiles > blockIdx.x ? (a.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -850,34 +889,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp < TC_A_WARPS) {
     // ---------------- A producers ----------------
     // Warp w owns TMEM lane quarter q = w % 4 (tile rows 32 q .. 32 q + 31) and
-    // channel half h = w / 4 (16 channels) of every 32-channel k-block.
+    // TC_A_HALVES 16-channel halves, from half0, of every 32-channel sub-block.
     const int q = warp & 3;
-    const int half = warp >> 2;
+    const int half0 = (warp >> 2) * TC_A_HALVES;
     const uint32_t tm_rows = tmem + ((uint32_t)(q * 32) << 16);
     const uint32_t stage0 = smem_addr(smem);
     int st = 0;
     uint32_t par = 0;
     int lo_slot = 0;     // lo slot of the k-block being split
     uint32_t lo_par = 0;  // its fill phase parity
-    // Remainder of this warp's 32 rows x 16 channels of stage `st` into lo
-    // slot `lo_slot` once the lo issuer has freed it; false on a timeout.
-    auto split_into_slot = [&]() -> bool {
+    int kbt = 0;        // the k-block's index within its tile
+    // Remainder of this warp's 32 rows x 16 channels of each of the `nsub`
+    // sub-blocks of stage `st` into lo slot `lo_slot` once the lo issuer has
+    // freed it; false on a timeout.
+    auto split_into_slot = [&](int nsub) -> bool {
       if (!mbar_wait(&B.lo_empty[lo_slot], lo_par ^ 1u, TC_ERR_WAIT_EMPTY)) return false;
       tc_fence_after();
-      float lo[16];
       const uint32_t tile_s = stage0 + (uint32_t)st * L.stage_bytes;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        float4 v;
-        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                     : "r"(tile_s + sw128_off(q * 32 + lane, half * 4 + c4)));
-        lo[4 * c4 + 0] = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-        lo[4 * c4 + 1] = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-        lo[4 * c4 + 2] = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-        lo[4 * c4 + 3] = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+      for (int j = 0; j < KS; ++j) {
+        if (j >= nsub) break;
+#pragma unroll
+        for (int hh = 0; hh < TC_A_HALVES; ++hh) {
+          const int half = half0 + hh;
+          float lo[16];
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            float4 v;
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                         : "r"(tile_s + (uint32_t)j * TC_A_BYTES + sw128_off(q * 32 + lane, half * 4 + c4)));
+            lo[4 * c4 + 0] = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+            lo[4 * c4 + 1] = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+            lo[4 * c4 + 2] = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+            lo[4 * c4 + 3] = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+          }
+          tmem_st16(tm_rows + (uint32_t)lo_slot * slot_cols + (uint32_t)(j * TC_LO_COLS + half * 16), lo);
+        }
       }
-      tmem_st16(tm_rows + (uint32_t)(lo_slot * TC_LO_COLS + half * 16), lo);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(&B.lo_full[lo_slot]);
@@ -888,15 +937,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       return true;
     };
     if (a.amode == TC_A_GATHER) {
-      // Gather: 16-byte cp.async of this warp's 32 rows x 64 B into the
+      // Gather: 16-byte cp.async of this warp's 32 rows x 64 B per half into the
       // swizzled A tile, zero-filled for padding taps, rows outside the output
       // and padded channels, run `ahead` k-blocks in front of the split.
       const int lrow = lane >> 2;
       const int lchunk = lane & 3;
-      const int lane_c = half * 16 + lchunk * 4;
       const int ahead = S - 1;  // k-blocks loaded beyond the one being split
       int64_t ltile = blockIdx.x;
-      int lkr = 0, lks = 0, lcb = 0;
+      int lkb = 0;                    // the load cursor's k-block within its tile
+      int lkr = 0, lks = 0, lcb = 0;  // and its next sub-block (tap row, tap column, channel block)
       int lst = 0;
       uint32_t lpar = 0;
       int roff[4];  // element offsets (the input spans < 2^31 elements; checked on the host)
@@ -910,29 +959,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           // Rows outside the output get a coordinate that fails the bounds test.
           ih0[i] = ok ? oh_ * a.sh - a.ph : -0x40000000;
           iw0[i] = ow_ * a.sw - a.pw;
-          roff[i] = ok ? n_ * (int)a.xs0 + ih0[i] * (int)a.xs2 + iw0[i] * (int)a.xs3 + lane_c : 0;
+          roff[i] = ok ? n_ * (int)a.xs0 + ih0[i] * (int)a.xs2 + iw0[i] * (int)a.xs3 : 0;
         }
       };
       bool alive = true;
       // Issue the copies of the load cursor's k-block and advance the cursor.
       auto load_next = [&]() -> bool {
         if (!mbar_wait(&empty[lst], lpar ^ 1u, TC_ERR_WAIT_EMPTY)) return false;
-
-        const int dy = lkr * a.dh, dx = lks * a.dw;
-        const int cbase = lcb * TC_BK;
-        const bool cok = cbase + lane_c < a.c;
-        const int koff = dy * (int)a.xs2 + dx * (int)a.xs3 + cbase;
+        const int nsub = min(KS, a.sb_total - lkb * KS);
         const uint32_t tile_s = stage0 + (uint32_t)lst * L.stage_bytes;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = q * 32 + lrow + 8 * i;
-          const bool ok = cok && (unsigned)(ih0[i] + dy) < (unsigned)a.h &&
-                          (unsigned)(iw0[i] + dx) < (unsigned)a.w;
-          const float* src = a.x + (ok ? roff[i] + koff : 0);
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(
-                           tile_s + sw128_off(row, half * 4 + lchunk)),
-                       "l"(src), "r"(ok ? 16 : 0)
-                       : "memory");
+        for (int j = 0; j < KS; ++j) {
+          if (j >= nsub) break;
+          const int dy = lkr * a.dh, dx = lks * a.dw;
+          const int cbase = lcb * TC_BK;
+#pragma unroll
+          for (int hh = 0; hh < TC_A_HALVES; ++hh) {
+            const int half = half0 + hh;
+            const int lane_c = half * 16 + lchunk * 4;
+            const bool cok = cbase + lane_c < a.c;
+            const int koff = dy * (int)a.xs2 + dx * (int)a.xs3 + cbase + lane_c;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int row = q * 32 + lrow + 8 * i;
+              const bool ok = cok && (unsigned)(ih0[i] + dy) < (unsigned)a.h &&
+                              (unsigned)(iw0[i] + dx) < (unsigned)a.w;
+              const float* src = a.x + (ok ? roff[i] + koff : 0);
+              asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(
+                               tile_s + (uint32_t)j * TC_A_BYTES + sw128_off(row, half * 4 + lchunk)),
+                           "l"(src), "r"(ok ? 16 : 0)
+                           : "memory");
+            }
+          }
+          if (++lcb == a.cb) {
+            lcb = 0;
+            if (++lks == a.s) {
+              lks = 0;
+              ++lkr;
+            }
+          }
         }
         asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(
                          smem_addr(&full_x[lst]))
@@ -941,16 +1006,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           lst = 0;
           lpar ^= 1u;
         }
-        if (++lcb == a.cb) {
-          lcb = 0;
-          if (++lks == a.s) {
-            lks = 0;
-            if (++lkr == a.r) {
-              lkr = 0;
-              ltile += gridDim.x;
-              if (ltile < a.tiles) setup_rows();
-            }
-          }
+        if (++lkb == KB) {
+          lkb = 0;
+          lkr = lks = lcb = 0;
+          ltile += gridDim.x;
+          if (ltile < a.tiles) setup_rows();
         }
         return true;
       };
@@ -975,11 +1035,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // let the hi issuer read it.
         fence_proxy_async_smem();
         mbar_arrive(&B.fenced[st]);
-        if (!split_into_slot()) break;
+        if (!split_into_slot(min(KS, a.sb_total - kbt * KS))) break;
         if (++st == S) {
           st = 0;
           par ^= 1u;
         }
+        if (++kbt == KB) kbt = 0;
       }
       // No copy may land in shared memory after the CTA has exited.
       asm volatile("cp.async.wait_all;" ::: "memory");
@@ -987,11 +1048,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // TMA modes: the A tile arrives by TMA; only the remainder is computed.
       for (int64_t g = 0; g < total; ++g) {
         if (!mbar_wait(&full_x[st], par, TC_ERR_WAIT_A)) break;
-        if (!split_into_slot()) break;
+        if (!split_into_slot(min(KS, a.sb_total - kbt * KS))) break;
         if (++st == S) {
           st = 0;
           par ^= 1u;
         }
+        if (++kbt == KB) kbt = 0;
       }
     }
   } else if (warp == TC_WARP_TMA) {
@@ -1011,34 +1073,53 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             alive = false;
             break;
           }
+          const int nsub = min(KS, a.sb_total - kb * KS);
           if (elect_one()) {
             uint8_t* stage = smem + (size_t)st * L.stage_bytes;
             // TMA modes: A and both weight tiles complete on full_x; gather
             // mode: the weights on full_b (A arrives by the producers' cp.async).
-            uint64_t* bbar = a.amode == TC_A_GATHER ? &full_b[st] : &full_x[st];
-            if (a.amode == TC_A_FLAT) {
-              mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES + 2 * b_bytes);
-              tma_load_2d(stage, &amap, &full_x[st], cbk * TC_BK, t.m0);
-            } else if (a.amode == TC_A_RECT) {
-              // Taps outside the image read as zero (TMA out-of-bounds fill).
-              mbar_arrive_expect_tx(&full_x[st], TC_A_BYTES + 2 * b_bytes);
-              tma_load_4d(stage, &amap, &full_x[st], cbk * TC_BK, t.ow0 * a.sw - a.pw + ks * a.dw,
-                          t.oh0 * a.sh - a.ph + kr * a.dh, t.n);
-            } else {
-              mbar_arrive_expect_tx(&full_b[st], 2 * b_bytes);
+            const bool gmode = a.amode == TC_A_GATHER;
+            uint64_t* bbar = gmode ? &full_b[st] : &full_x[st];
+            mbar_arrive_expect_tx(bbar, (uint32_t)nsub * ((gmode ? 0u : TC_A_BYTES) + 2u * b_bytes));
+            int r_ = kr, s_ = ks, c_ = cbk;
+#pragma unroll
+            for (int j = 0; j < KS; ++j) {
+              if (j >= nsub) break;
+              uint8_t* at = stage + (size_t)j * TC_A_BYTES;
+              uint8_t* bt = stage + L.a_bytes + (size_t)j * 2 * b_bytes;
+              if (a.amode == TC_A_FLAT) {
+                tma_load_2d(at, &amap, &full_x[st], c_ * TC_BK, t.m0);
+              } else if (a.amode == TC_A_RECT) {
+                // Taps outside the image read as zero (TMA out-of-bounds fill).
+                tma_load_4d(at, &amap, &full_x[st], c_ * TC_BK, t.ow0 * a.sw - a.pw + s_ * a.dw,
+                            t.oh0 * a.sh - a.ph + r_ * a.dh, t.n);
+              }
+              const int sb = kb * KS + j;
+              tma_load_2d(bt, &wmap_hi, bbar, sb * TC_BK, n0);
+              tma_load_2d(bt + b_bytes, &wmap_lo, bbar, sb * TC_BK, n0);
+              if (++c_ == a.cb) {
+                c_ = 0;
+                if (++s_ == a.s) {
+                  s_ = 0;
+                  ++r_;
+                }
+              }
             }
-            tma_load_2d(stage + TC_A_BYTES, &wmap_hi, bbar, kb * TC_BK, n0);
-            tma_load_2d(stage + TC_A_BYTES + b_bytes, &wmap_lo, bbar, kb * TC_BK, n0);
           }
+          __syncwarp();
           if (++st == S) {
             st = 0;
             par ^= 1u;
           }
-          if (++cbk == a.cb) {
-            cbk = 0;
-            if (++ks == a.s) {
-              ks = 0;
-              ++kr;
+#pragma unroll
+          for (int j = 0; j < KS; ++j) {
+            if (j >= nsub) break;
+            if (++cbk == a.cb) {
+              cbk = 0;
+              if (++ks == a.s) {
+                ks = 0;
+                ++kr;
+              }
             }
           }
         }
@@ -1053,9 +1134,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else if (warp == TC_WARP_HI) {
-    tc_issue<0>(a, smem, L, tmem, B);
+    tc_issue<0, KS>(a, smem, L, tmem, B);
   } else if (warp == TC_WARP_LO) {
-    tc_issue<1>(a, smem, L, tmem, B);
+    tc_issue<1, KS>(a, smem, L, tmem, B);
   } else if (warp >= TC_WARP_EPI) {
     // ---------------- promotion (fp32 RN adds) + epilogue ----------------
     // Two warps per TMEM lane quarter; warp half h owns the 16-column chunks
@@ -1288,23 +1369,28 @@ bool aligned16(const void* p) { return (((uintptr_t)p) & 15) == 0; }
 // opt-in maximum minus the kernel's static shared memory.
 using TcKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                           const TcArgs);
-constexpr int TC_VARIANTS = 12;  // 4 activations x 3 residual modes
+constexpr int TC_VARIANTS = 24;  // 4 activations x 3 residual modes x 2 k-block widths
 
-template <int ACT>
+template <int ACT, int KS>
 TcKernel tc_kernel_rm(int rm) {
-  return rm == 1 ? conv_tc_kernel<ACT, 1> : rm == 2 ? conv_tc_kernel<ACT, 2> : conv_tc_kernel<ACT, 0>;
+  return rm == 1 ? conv_tc_kernel<ACT, 1, KS> : rm == 2 ? conv_tc_kernel<ACT, 2, KS> : conv_tc_kernel<ACT, 0, KS>;
 }
 
-// Variant v = 3 * act + rm; activation codes other than the four named ones
-// apply no activation.
-TcKernel tc_kernel(int v) {
-  const int act = v / 3, rm = v % 3;
+template <int KS>
+TcKernel tc_kernel_ks(int act, int rm) {
   switch (act) {
-    case MM_ACT_RELU: return tc_kernel_rm<MM_ACT_RELU>(rm);
-    case MM_ACT_SILU: return tc_kernel_rm<MM_ACT_SILU>(rm);
-    case MM_ACT_SIGMOID: return tc_kernel_rm<MM_ACT_SIGMOID>(rm);
-    default: return tc_kernel_rm<MM_ACT_NONE>(rm);
+    case MM_ACT_RELU: return tc_kernel_rm<MM_ACT_RELU, KS>(rm);
+    case MM_ACT_SILU: return tc_kernel_rm<MM_ACT_SILU, KS>(rm);
+    case MM_ACT_SIGMOID: return tc_kernel_rm<MM_ACT_SIGMOID, KS>(rm);
+    default: return tc_kernel_rm<MM_ACT_NONE, KS>(rm);
   }
+}
+
+// Variant v = 2 * (3 * act + rm) + (ksub == 2); activation codes other than
+// the four named ones apply no activation.
+TcKernel tc_kernel(int v) {
+  const int ks2 = v & 1, act = (v >> 1) / 3, rm = (v >> 1) % 3;
+  return ks2 ? tc_kernel_ks<2>(act, rm) : tc_kernel_ks<1>(act, rm);
 }
 
 int tc_smem_limit(int dev, size_t* out) {
@@ -1396,7 +1482,7 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   if (k_out > TC_MAX_BIAS) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: too many output channels");
   a.m_total = (int)m_total;
   a.cb = c_pad / TC_BK;
-  a.kb_total = r * s * a.cb;
+  a.sb_total = r * s * a.cb;
   // N tiles of at most TC_MAX_BN channels, balanced (128 -> 2 x 64, 144 -> 2 x 80).
   {
     const int ntiles = (k_out + TC_MAX_BN - 1) / TC_MAX_BN;
@@ -1404,13 +1490,27 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
     a.bn = ((per + 15) / 16) * 16;
   }
   a.n_tiles = (k_out + a.bn - 1) / a.bn;
-  // Promotion period: at most 12 k-blocks (48 MMAs per accumulator), balanced
-  // over the tile (18 -> 2 x 9, 36 -> 3 x 12).  The tensor core's truncating
-  // accumulation biases one period's sum by up to ~2.5e-6 relative
+  // Sub-blocks per k-block: every k-block costs each warp role a fixed chain
+  // of barrier waits, copies and MMA issues, so reductions of at least four
+  // 32-channel sub-blocks run two per k-block (measured 4-11 % faster on the
+  // 3x3 layers of YOLOv8n at batch 64; one per k-block stays faster for
+  // reductions of one or two sub-blocks, where a tile then has two k-blocks
+  // to overlap instead of one).
+  a.ksub = a.sb_total >= 4 ? 2 : 1;
+  if (const char* env = std::getenv("MATRIXMAN_TC_KSUB")) {
+    const int v = std::atoi(env);
+    if (v == 1 || v == 2) a.ksub = v;
+  }
+  while (a.ksub > 1 && a.ksub / 2 >= a.sb_total) a.ksub /= 2;  // no k-block of padding only
+  a.kb_total = (a.sb_total + a.ksub - 1) / a.ksub;
+  // Promotion period: at most 12 sub-blocks (48 MMAs per accumulator),
+  // balanced over the tile (18 -> 2 x 9, 36 -> 3 x 12).  The tensor core's
+  // truncating accumulation biases one period's sum by up to ~2.5e-6 relative
   // (all-positive data); promotion into the fp32 total keeps that bias from
   // growing with the reduction length.
   {
-    const int np = (a.kb_total + 11) / 12;
+    const int pmax = 12 / a.ksub;
+    const int np = (a.kb_total + pmax - 1) / pmax;
     a.period = (a.kb_total + np - 1) / np;
   }
   a.act = p->act;
@@ -1519,15 +1619,26 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   // else one; as many lo slots as fit, up to TC_MAX_LO.  Shared memory: as
   // many A + B stages as fit (the lo ring no longer bounds them).
   a.xbuf = 0;
-  for (int xbuf = 2; xbuf >= 1 && a.xbuf == 0; --xbuf) {
-    const int free_cols = (int)TC_TMEM_COLS - (4 + xbuf) * a.bn;
-    const int slots = free_cols / TC_LO_COLS;
-    if (slots >= 2) {
-      a.xbuf = xbuf;
-      a.lo_slots = slots < TC_MAX_LO ? slots : TC_MAX_LO;
+  // (fewer sub-blocks per k-block when TMEM cannot hold two slots of the
+  // requested width)
+  for (; a.xbuf == 0 && a.ksub >= 1; a.ksub /= 2) {
+    for (int xbuf = 2; xbuf >= 1 && a.xbuf == 0; --xbuf) {
+      const int free_cols = (int)TC_TMEM_COLS - (4 + xbuf) * a.bn;
+      const int slots = free_cols / (TC_LO_COLS * a.ksub);
+      if (slots >= 2) {
+        a.xbuf = xbuf;
+        a.lo_slots = slots < TC_MAX_LO ? slots : TC_MAX_LO;
+      }
     }
+    if (a.xbuf != 0) break;
   }
   if (a.xbuf == 0) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: N tile too wide");
+  a.kb_total = (a.sb_total + a.ksub - 1) / a.ksub;
+  {
+    const int pmax = 12 / a.ksub;
+    const int np = (a.kb_total + pmax - 1) / pmax;
+    a.period = (a.kb_total + np - 1) / np;
+  }
   if (const char* lo_env = std::getenv("MATRIXMAN_TC_LO_SLOTS")) {
     const int v = std::atoi(lo_env);
     if (v >= 2 && v <= a.lo_slots) a.lo_slots = v;
@@ -1539,7 +1650,7 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   }
   int stages = 0;
   for (int st = max_stages; st >= 2; --st) {
-    if (TcSmem::make(a.bn, st, k_out, stg_bound).bytes() <= smem_limit) {
+    if (TcSmem::make(a.bn, a.ksub, st, k_out, stg_bound).bytes() <= smem_limit) {
       stages = st;
       break;
     }
@@ -1549,7 +1660,7 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   a.epi_groups = (a.period >= a.kb_total && a.xbuf == 2 && a.bn <= 16 * TC_EPI_CHUNKS) ? 2 : 1;
   a.stg_chunks = staged ? (a.epi_groups == 2 ? nchunk : (nchunk + 1) / 2) : 0;
   const int64_t ktot = (int64_t)r * s * c_pad;
-  size_t smem = TcSmem::make(a.bn, stages, k_out, a.stg_chunks).bytes();
+  size_t smem = TcSmem::make(a.bn, a.ksub, stages, k_out, a.stg_chunks).bytes();
 
   CUtensorMap mhi, mlo;
   if ((rc = weight_map(w_hi, ktot, k_pad, a.bn, &mhi)) != MM_OK) return rc;
@@ -1557,8 +1668,9 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   // The kernel owns all 512 TMEM columns, so a second resident CTA on an SM
   // would stall in tcgen05.alloc until the first exits: pad the shared-memory
   // request whenever the occupancy calculator allows more than one CTA.
-  const int variant = 3 * (a.act >= 0 && a.act <= MM_ACT_SIGMOID ? a.act : MM_ACT_NONE) +
-                      (a.res ? (a.res_before_act ? 1 : 2) : 0);
+  const int variant = 2 * (3 * (a.act >= 0 && a.act <= MM_ACT_SIGMOID ? a.act : MM_ACT_NONE) +
+                           (a.res ? (a.res_before_act ? 1 : 2) : 0)) +
+                      (a.ksub == 2 ? 1 : 0);
   const TcKernel kernel = tc_kernel(variant);
   {
     static size_t configured[256][TC_VARIANTS] = {};
