@@ -235,6 +235,18 @@ int mm_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
 int mm_memcpy_peer(void* dst, int dst_device, const void* src, int src_device, size_t bytes,
                    void* stream);
 int mm_enable_peer_access(int device, int peer);
+/* Device memory shared between processes, one process per GPU (no counterpart
+ * in the reference, which drives device 0 only).  mm_ipc_alloc allocates
+ * `bytes` on `device` and writes its CUDA IPC handle (64 bytes) to handle_out;
+ * another process passes the handle to mm_ipc_open (on its own device) and
+ * gets a pointer it may copy into with mm_memcpy_d2d (copy engines over
+ * NVLink); mm_ipc_close unmaps it; the owner frees with mm_ipc_free after
+ * every opener has closed it. */
+#define MM_IPC_HANDLE_BYTES 64
+int mm_ipc_alloc(int device, size_t bytes, void** ptr_out, void* handle_out);
+int mm_ipc_free(int device, void* ptr);
+int mm_ipc_open(int device, const void* handle, void** ptr_out);
+int mm_ipc_close(int device, void* ptr);
 /* Page-locked host buffers for asynchronous transfers. */
 int mm_host_alloc_pinned(size_t bytes, void** out);
 int mm_host_free_pinned(void* ptr);

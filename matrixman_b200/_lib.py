@@ -25,6 +25,7 @@ MM_ERR_STATE = 6
 MM_F32 = 0
 MM_I64 = 1
 
+MM_IPC_HANDLE_BYTES = 64
 POOL_ACTIVATION = 0
 POOL_SCRATCH = 1
 POOL_PARAMETER = 2
@@ -174,6 +175,10 @@ SIGNATURES = {
     "mm_conv2d_tc": [_T, _fp, _fp, _i, _i, _i, _i, _i, _i, _fp, _T,
                      ctypes.POINTER(MMConvParams), _T, _vp],
     "mm_tf32_split": [_fp, _fp, _fp, _i64, _vp],
+    "mm_ipc_alloc": [_i, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _vp],
+    "mm_ipc_free": [_i, _vp],
+    "mm_ipc_open": [_i, _vp, ctypes.POINTER(ctypes.c_void_p)],
+    "mm_ipc_close": [_i, _vp],
     "mm_kernel_error": [_i, ctypes.POINTER(_i), _i],
     "mm_gemm": [_T, _T, _T, _d, _d, _i, _T, _vp],
     "mm_yolo_decode": [_TT, ctypes.POINTER(ctypes.c_float), _i, _i, _i, _T, _vp],

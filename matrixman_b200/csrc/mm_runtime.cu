@@ -600,6 +600,65 @@ extern "C" int mm_enable_peer_access(int device, int peer) {
   return MM_OK;
 }
 
+// Device memory shared between processes (one process per GPU): the owner
+// allocates it and exports a CUDA IPC handle; the other processes open the
+// handle and write into it with copy-engine copies (NVLink between GPUs).
+extern "C" int mm_ipc_alloc(int device, size_t bytes, void** ptr_out, void* handle_out) {
+  if (ptr_out == nullptr || handle_out == nullptr || bytes == 0)
+    return fail(MM_ERR_INVALID, "mm_ipc_alloc: bad arguments");
+  int prev = current_device();
+  MM_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) {
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e == cudaSuccess) {
+      memcpy(handle_out, &h, sizeof(h));
+      *ptr_out = p;
+    } else {
+      cudaFree(p);
+    }
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "mm_ipc_alloc");
+  return MM_OK;
+}
+
+extern "C" int mm_ipc_free(int device, void* ptr) {
+  if (ptr == nullptr) return MM_OK;
+  int prev = current_device();
+  MM_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  cudaError_t e = cudaFree(ptr);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "mm_ipc_free");
+  return MM_OK;
+}
+
+extern "C" int mm_ipc_open(int device, const void* handle, void** ptr_out) {
+  if (ptr_out == nullptr || handle == nullptr) return fail(MM_ERR_INVALID, "mm_ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  int prev = current_device();
+  MM_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "mm_ipc_open");
+  *ptr_out = p;
+  return MM_OK;
+}
+
+extern "C" int mm_ipc_close(int device, void* ptr) {
+  if (ptr == nullptr) return MM_OK;
+  int prev = current_device();
+  MM_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "mm_ipc_close");
+  return MM_OK;
+}
+
 extern "C" int mm_host_alloc_pinned(size_t bytes, void** out) {
   MM_CUDA(cudaHostAlloc(out, bytes, cudaHostAllocPortable), "cudaHostAlloc");
   return MM_OK;

@@ -12,9 +12,13 @@ the final gather of the per-replica outputs:
   each device's stream back to back and run concurrently; their outputs are
   copied into one buffer on the root device with copy-engine peer copies
   (NVLink when peer access is available), ordered by cross-device events.
-* ``gather_to_root`` (one process per device, e.g. under torchrun): rank
-  outputs travel to rank 0 with point-to-point sends over the process group
-  (NCCL over NVLink for device memory, gloo for CPU tensors in tests).
+* ``PeerGather`` (one process per device, e.g. under torchrun): rank 0's
+  gather buffers are shared through CUDA IPC and every rank writes its rows
+  with copy-engine copies over NVLink on a side stream, so a step's gather
+  overlaps the next step's forward and uses no SMs.
+* ``gather_to_root`` (one process per device): rank outputs travel to rank 0
+  with point-to-point sends over the process group (NCCL over NVLink for
+  device memory, gloo for CPU tensors in tests).
 """
 
 from __future__ import annotations
@@ -273,3 +277,161 @@ def gather_to_root(local, batch_sizes: list[int], group=None, root: int = 0):
         if stream_ctx is not None:
             stream_ctx.__exit__(None, None, None)
     return out
+
+
+class _IpcBlock(runtime.DeviceStorage):
+    """A gather buffer allocated for sharing with other processes (CUDA IPC);
+    freed with mm_ipc_free instead of returning to the arena."""
+
+    __slots__ = ()
+
+    def release(self) -> None:
+        if self._released or self.pointer == 0:
+            return
+        self._released = True
+        if self.runtime.closed:
+            return
+        _lib.load().mm_ipc_free(self.runtime.index, ctypes.c_void_p(self.pointer))
+
+
+class PeerGather:
+    """Gather of every rank's batch-major output into one buffer on the root's
+    GPU by copy engines, one process per GPU (e.g. under torchrun).
+
+    The root allocates ``slots`` gather buffers and exports them through CUDA
+    IPC; every rank opens them once.  ``push(local)`` copies this rank's dense
+    output into its rows of the current slot with ``cudaMemcpyAsync`` on a copy
+    stream of the rank's own, ordered after the output's producer by an event.
+    The copies use copy engines over NVLink, not SMs, so they overlap the next
+    forward (a process-group collective would occupy SMs that the persistent
+    convolution kernels expect to have).  A pushed output stays referenced
+    until its copy has completed.  ``collect()`` waits for this rank's copies,
+    then meets the other ranks at a process-group barrier; on the root it
+    returns the gathered batch of the last push, valid until the next
+    ``collect()``.  Every rank takes the same steps in the same order."""
+
+    def __init__(self, tail_shape, batch_sizes: list[int], group=None, root: int = 0,
+                 slots: int = 2, device: int | None = None):
+        self.group = group
+        self.root = int(root)
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if len(batch_sizes) != self.world:
+            raise ValueError("MatrixMan: one batch size per rank is required")
+        if slots < 1:
+            raise ValueError("MatrixMan: at least one gather slot is required")
+        self.tail = tuple(int(v) for v in tail_shape)
+        self.sizes = [int(b) for b in batch_sizes]
+        self.total = sum(self.sizes)
+        self.offsets = [sum(self.sizes[:r]) for r in range(self.world)]
+        row = 1
+        for v in self.tail:
+            row *= v
+        self.row_bytes = row * 4
+        self.device = runtime.current_device() if device is None else int(device)
+        self.rt = runtime.get_runtime(self.device)
+        lib = _lib.load()
+        self.lib = lib
+        nbytes = max(self.total * self.row_bytes, 1)
+        self.blocks: list[_IpcBlock] = []
+        handles = []
+        if self.rank == self.root:
+            for _ in range(slots):
+                ptr = ctypes.c_void_p()
+                h = ctypes.create_string_buffer(_lib.MM_IPC_HANDLE_BYTES)
+                _lib.check(lib.mm_ipc_alloc(self.device, nbytes, ctypes.byref(ptr), h), "gather buffer")
+                self.blocks.append(_IpcBlock(self.rt, ptr.value, nbytes, torch.float32,
+                                             _lib.POOL_ACTIVATION))
+                handles.append(h.raw)
+        obj = [handles]
+        dist.broadcast_object_list(obj, src=self.root, group=group)
+        if self.rank == self.root:
+            self.dst = [b.pointer for b in self.blocks]
+        else:
+            self.dst = []
+            for raw in obj[0]:
+                ptr = ctypes.c_void_p()
+                _lib.check(lib.mm_ipc_open(self.device, ctypes.create_string_buffer(raw, len(raw)),
+                                           ctypes.byref(ptr)), "open gather buffer")
+                self.dst.append(ptr.value)
+        s = ctypes.c_void_p()
+        _lib.check(lib.mm_stream_create(self.device, ctypes.byref(s)), "copy stream")
+        self.copy_stream = s.value
+        self.ready = [_Event(self.device) for _ in range(slots)]
+        self.done = [_Event(self.device) for _ in range(slots)]
+        self.kept: list = [None] * slots
+        self.slot = 0
+        self.last = -1
+        runtime.set_device(self.device)
+
+    def push(self, local: MatrixManTensor) -> None:
+        if not isinstance(local, MatrixManTensor):
+            raise TypeError("MatrixMan: PeerGather pushes MatrixMan tensors")
+        if tuple(int(v) for v in local.shape) != (self.sizes[self.rank],) + self.tail:
+            raise ValueError("MatrixMan: local output does not match this rank's slice shape")
+        lib = self.lib
+        s = self.slot
+        if self.kept[s] is not None:
+            # The copy that last used this slot must be done before its source
+            # block may return to the arena.
+            _lib.check(lib.mm_event_sync(self.done[s].handle, runtime.config.waitTimeoutMs),
+                       "gather copy wait")
+            self.kept[s] = None
+        local = _dense(local)
+        _lib.check(lib.mm_event_record(self.ready[s].handle, local.runtime.stream), "event record")
+        _lib.check(lib.mm_stream_wait_event(self.copy_stream, self.ready[s].handle), "stream wait")
+        nbytes = self.sizes[self.rank] * self.row_bytes
+        if nbytes:
+            dst = self.dst[s] + self.offsets[self.rank] * self.row_bytes
+            _lib.check(lib.mm_memcpy_d2d(ctypes.c_void_p(dst), ctypes.c_void_p(local.element_ptr),
+                                         nbytes, self.copy_stream), "gather copy")
+        _lib.check(lib.mm_event_record(self.done[s].handle, self.copy_stream), "event record")
+        self.kept[s] = local
+        self.last = s
+        self.slot = (s + 1) % len(self.dst)
+
+    def join(self, stream) -> None:
+        """Make `stream` wait for this rank's last copy (device-side)."""
+        if self.last >= 0:
+            _lib.check(self.lib.mm_stream_wait_event(stream, self.done[self.last].handle), "stream wait")
+
+    def collect(self):
+        """Wait for this rank's copies, meet the other ranks; the root gets the
+        gathered batch of the last push (None elsewhere)."""
+        _lib.check(self.lib.mm_stream_sync(self.copy_stream, runtime.config.waitTimeoutMs),
+                   "gather copies")
+        for i in range(len(self.kept)):
+            self.kept[i] = None
+        _barrier(self.group, self.device)
+        if self.rank != self.root or self.last < 0:
+            return None
+        block = self.blocks[self.last]
+        shape = (self.total,) + self.tail
+        return MatrixManTensor(block, shape, 0, contiguous_strides(shape))
+
+    def close(self) -> None:
+        """Unmap (other ranks) after a final collect; the root frees its
+        buffers when they are garbage-collected."""
+        if self.rank != self.root:
+            for p in self.dst:
+                self.lib.mm_ipc_close(self.device, ctypes.c_void_p(p))
+            self.dst = []
+        if self.copy_stream:
+            self.lib.mm_stream_destroy(ctypes.c_void_p(self.copy_stream))
+            self.copy_stream = None
+
+
+def _barrier(group, device: int) -> None:
+    """Process-group barrier; with NCCL an all-reduce of a CUDA tensor on the
+    rank's own device (dist.barrier would place its tensor on the default
+    accelerator, which is the matrixman device once the backend is up)."""
+    try:
+        nccl = dist.get_backend(group) == "nccl"
+    except Exception:
+        nccl = False
+    if nccl:
+        t = torch.zeros(1, device=torch.device("cuda", device))
+        dist.all_reduce(t, group=group)
+        torch.cuda.synchronize(device)
+    else:
+        dist.barrier(group=group)
