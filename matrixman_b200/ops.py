@@ -627,7 +627,10 @@ def reduce(x, dims, keepdim=False, mean=True) -> MatrixManTensor:
     return MatrixManTensor._from_owner(y._owner, shape, 0, contiguous_strides(shape))
 
 
-def upsample_nearest2d(x, output_size, scales_h=None, scales_w=None) -> MatrixManTensor:
+def upsample_nearest2d(x, output_size, scales_h=None, scales_w=None,
+                       out: MatrixManTensor | None = None) -> MatrixManTensor:
+    """Nearest upsample; ``out`` (optional) is a view to write into, e.g. a
+    channel slice of a concatenation buffer."""
     x = require_mm(x, "upsample_nearest2d")
     require_f32(x, "upsample_nearest2d")
     if x.dim() != 4:
@@ -640,7 +643,12 @@ def upsample_nearest2d(x, output_size, scales_h=None, scales_w=None) -> MatrixMa
     else:
         oh, ow = (int(v) for v in output_size)
     shape = (n, c, oh, ow)
-    y = empty(x.runtime, shape, _out_strides_like(x, shape))
+    if out is not None:
+        if tuple(int(v) for v in out.shape) != shape:
+            raise ValueError("MatrixMan/CUDA: upsample_nearest2d output view has the wrong shape")
+        y = out
+    else:
+        y = empty(x.runtime, shape, _out_strides_like(x, shape))
     _launch("mm_upsample_nearest2d", _p(x.desc()), float(scales_h or 0.0), float(scales_w or 0.0),
             _p(y.desc()), _stream(x))
     return y

@@ -419,7 +419,11 @@ class PreparedC2f(nn.Module):
         self.shortcut = [bool(getattr(b, "add", False)) for b in module.m]
         _copy_routing_attrs(self, source)
 
-    def forward(self, x):
+    @property
+    def out_channels(self) -> int:
+        return self.cv2.out_channels
+
+    def forward(self, x, out=None):
         n_, _, h, w = (int(v) for v in x.shape)
         k = len(self.m)
         c = self.c
@@ -431,7 +435,7 @@ class PreparedC2f(nn.Module):
             t = blk.cv1(inp)
             blk.cv2(t, out=_channel_slice(buf, (2 + i) * c, (3 + i) * c),
                     residual=inp if self.shortcut[i] else None)
-        return self.cv2(buf)
+        return self.cv2(buf, out=out)
 
 
 class _BottleneckPair(nn.Module):
@@ -451,7 +455,11 @@ class PreparedSPPF(nn.Module):
         self.cv2 = cv2
         _copy_routing_attrs(self, source)
 
-    def forward(self, x):
+    @property
+    def out_channels(self) -> int:
+        return self.cv2.out_channels
+
+    def forward(self, x, out=None):
         n_, _, h, w = (int(v) for v in x.shape)
         c = self.cv1.out_channels
         shape = (n_, 4 * c, h, w)
@@ -461,7 +469,7 @@ class PreparedSPPF(nn.Module):
         s1, s2, s3 = (_channel_slice(buf, i * c, (i + 1) * c) for i in (1, 2, 3))
         ops._launch("mm_sppf_pool", ops._p(s0.desc()), ops._p(s1.desc()), ops._p(s2.desc()),
                     ops._p(s3.desc()), x.runtime.stream)
-        return self.cv2(buf)
+        return self.cv2(buf, out=out)
 
 
 class PreparedDetect(nn.Module):
@@ -535,6 +543,88 @@ class PreparedResBottleneck(nn.Module):
     def forward(self, x):
         identity = x if self.downsample is None else self.downsample(x)
         return self.conv3(self.conv2(self.conv1(x)), residual=identity, residual_before_act=True)
+
+
+class PreparedYOLOv8(nn.Module):
+    """Whole-model forward of a YOLOv8-architecture detector (backbone
+    b0..b9, PAN neck n12..n21 with nearest 2x upsamples and four
+    concatenations, Detect head) with every concatenation written in place:
+    each of the four neck concat buffers is allocated before its first
+    producer runs, and the producers -- the C2f and SPPF outputs, the two
+    upsamples and the two stride-2 neck convolutions -- write their channel
+    slices of it directly; consumers read those slices as views.  The
+    unprepared forward materialises each concatenation with a copy.
+
+    Concatenation layout (channels, in torch.cat order):
+      cat12 = [up(p5) | p4] at P4, cat15 = [up(n12) | p3] at P3,
+      cat18 = [n16(n15) | n12] at P4, cat21 = [n19(n18) | p5] at P5."""
+
+    def __init__(self, model: nn.Module, source=None):
+        super().__init__()
+        self.m = model
+        up = model.up
+        self.scale = float(up.scale_factor if not isinstance(up.scale_factor, tuple) else up.scale_factor[0])
+        _copy_routing_attrs(self, source)
+
+    @staticmethod
+    def eligible(model: nn.Module) -> bool:
+        names = ("b0", "b1", "b2", "b3", "b4", "b5", "b6", "b7", "b8", "b9", "up", "n12", "n15",
+                 "n16", "n18", "n19", "n21", "detect")
+        if type(model).__name__ != "YOLOv8" or not all(hasattr(model, n) for n in names):
+            return False
+        convs = ("b0", "b1", "b3", "b5", "b7", "n16", "n19")
+        c2fs = ("b2", "b4", "b6", "b8", "n12", "n15", "n18", "n21")
+        up = model.up
+        return (all(isinstance(getattr(model, n), PreparedConv2d) for n in convs)
+                and all(isinstance(getattr(model, n), PreparedC2f) for n in c2fs)
+                and isinstance(model.b9, PreparedSPPF) and isinstance(model.detect, PreparedDetect)
+                and isinstance(up, nn.Upsample) and up.mode == "nearest" and up.size is None
+                and up.scale_factor is not None
+                and float(up.scale_factor if not isinstance(up.scale_factor, tuple)
+                          else up.scale_factor[0]) == 2.0)
+
+    def __getattr__(self, name):
+        # The wrapped model's layers stay reachable (prepared.b2, .detect, ...).
+        try:
+            return super().__getattr__(name)
+        except AttributeError:
+            return getattr(self._modules["m"], name)
+
+    def _up(self, x, out):
+        n_, c, h, w = (int(v) for v in x.shape)
+        return ops.upsample_nearest2d(x, (int(h * self.scale), int(w * self.scale)), self.scale,
+                                      self.scale, out=out)
+
+    def forward(self, x):
+        m = self.m
+        c_p3, c_p4, c_p5 = m.b4.out_channels, m.b6.out_channels, m.b9.out_channels
+        c_n12, c_n16, c_n19 = m.n12.out_channels, m.n16.out_channels, m.n19.out_channels
+        rt = x.runtime
+
+        def cat_buffer(like, channels):
+            n_, _, h, w = (int(v) for v in like.shape)
+            shape = (n_, channels, h, w)
+            return ops.empty(rt, shape, _nhwc(shape))
+
+        t = m.b3(m.b2(m.b1(m.b0(x))))
+        cat15 = cat_buffer(t, c_n12 + c_p3)
+        p3 = m.b4(t, out=_channel_slice(cat15, c_n12, c_n12 + c_p3))
+        t = m.b5(p3)
+        cat12 = cat_buffer(t, c_p5 + c_p4)
+        p4 = m.b6(t, out=_channel_slice(cat12, c_p5, c_p5 + c_p4))
+        t = m.b8(m.b7(p4))
+        cat21 = cat_buffer(t, c_n19 + c_p5)
+        p5 = m.b9(t, out=_channel_slice(cat21, c_n19, c_n19 + c_p5))
+        self._up(p5, _channel_slice(cat12, 0, c_p5))
+        cat18 = cat_buffer(cat12, c_n16 + c_n12)
+        n12 = m.n12(cat12, out=_channel_slice(cat18, c_n16, c_n16 + c_n12))
+        self._up(n12, _channel_slice(cat15, 0, c_n12))
+        n15 = m.n15(cat15)
+        m.n16(n15, out=_channel_slice(cat18, 0, c_n16))
+        n18 = m.n18(cat18)
+        m.n19(n18, out=_channel_slice(cat21, 0, c_n19))
+        n21 = m.n21(cat21)
+        return m.detect([n15, n18, n21])
 
 
 def _downsample_unit(ds):
@@ -804,6 +894,9 @@ def _prepare_model(model: nn.Module, *, inplace: bool, diagnostics: bool) -> nn.
     _fold_all(target, report, _alias_counts(target))
     if config.preparedExecution:
         _replace(target, report, _alias_counts(target))
+        if PreparedYOLOv8.eligible(target):
+            target = PreparedYOLOv8(target, source=target)
+            report.block_units_prepared["YOLOv8 in-place neck"] += 1
     report.remaining_batch_norm_modules = sum(isinstance(m, nn.BatchNorm2d) for m in target.modules())
     target.eval()
     if diagnostics:

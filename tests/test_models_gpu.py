@@ -55,6 +55,23 @@ def test_yolov8n_prepared(mm, batch):
     assert rep.folded == 57 and rep.detection_head_prepared == 1
 
 
+def test_yolov8n_neck_concatenations_in_place(mm):
+    """The prepared YOLOv8 writes its four neck concatenations in place: a
+    prepared forward launches no concatenation copy, and matches the oracle
+    at a size whose levels are not powers of two (odd P5)."""
+    from matrixman_b200 import telemetry
+    model = W.yolov8_model("n")
+    x = W.yolo_input(2, seed=21, size=352)
+    p = mm.prepare(model)
+    assert p._matrixman_preparation_report.block_units_prepared["YOLOv8 in-place neck"] == 1
+    ref = run_cpu(model, x)
+    with torch.no_grad():
+        before = telemetry.launches["mm_cat"]
+        y = p(mm.to_device(x)).cpu()  # eager (first call)
+        assert telemetry.launches["mm_cat"] == before
+    assert max_rel_err(y, ref) < CONV_GEMM_REL
+
+
 def test_yolov8n_prepared_bs64(mm):
     """The benchmark's own configuration: YOLOv8n 640x640 at 64 images, eager
     forward, graph capture and graph replay, each against the CPU oracle."""
