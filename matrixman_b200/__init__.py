@@ -32,7 +32,7 @@ from .api import (
     to_gm45,
     unsupported_report,
 )
-from .pipeline import infer
+from .pipeline import infer, infer_stream
 from .detect import postprocess_detections
 from .frames import preprocess_frames
 from .preparation import auto_prepare, prepare, prepare_cuda, prepare_opengl
@@ -100,6 +100,7 @@ sys.modules[__name__].__class__ = _MatrixManModule
 
 __all__ = [
     "infer",
+    "infer_stream",
     "postprocess_detections",
     "preprocess_frames",
     "MatrixManTensor", "Gm45Tensor", "auto_prepare", "config", "debug_enabled", "device_count",

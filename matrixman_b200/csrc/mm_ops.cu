@@ -893,7 +893,25 @@ static int copy_impl(const mm_tensor_t* x_in, const mm_tensor_t* y_in, cudaStrea
   if (n == 0) return MM_OK;
   size_t es = x->dtype == MM_F32 ? 4 : 8;
   if (is_flat(g[0]) && is_flat(g[1])) {
-    MM_CUDA(cudaMemcpyAsync(y->data, x->data, n * es, cudaMemcpyDeviceToDevice, s), "mm_copy");
+    // Dense copies run on the SMs (as one row of the row-copy kernel), not on
+    // a copy engine: a device-to-device cudaMemcpyAsync waits in the copy
+    // engine's queue behind host transfers issued earlier on other streams
+    // (the next batch's upload), which would hold up the forward behind it.
+    const int64_t bytes = n * (int64_t)es;
+    if (bytes % 16 == 0 && bytes / 16 <= 0x7fffffffLL &&
+        ((((uintptr_t)x->data) | ((uintptr_t)y->data)) & 15) == 0) {
+      const int64_t cols4 = bytes / 16;
+      int64_t blocks = (cols4 + 4 * 256 - 1) / (4 * 256);
+      const int64_t cap = (int64_t)sm_count() * 16;
+      if (blocks > cap) blocks = cap;
+      if (blocks < 1) blocks = 1;
+      MM_CUDA(launch_pdl(copy_rows_vec4_kernel, dim3((unsigned)blocks), dim3(256), 0, s, (const float*)x->data,
+                         (float*)y->data, (int64_t)1, (int)cols4, (int64_t)0, (int64_t)0),
+              "mm_copy launch");
+      MM_LAUNCH_CHECK("mm_copy launch");
+      return MM_OK;
+    }
+    MM_CUDA(cudaMemcpyAsync(y->data, x->data, bytes, cudaMemcpyDeviceToDevice, s), "mm_copy");
     return MM_OK;
   }
   // Row copies (channel slices of NHWC buffers): rank-2 collapsed geometry

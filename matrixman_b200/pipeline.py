@@ -179,3 +179,125 @@ def infer(model, x: torch.Tensor, chunks: int = 4, device=None, sizes=None) -> t
             ev.close()
     del keep
     return out
+
+
+def infer_stream(model, batches, device=None, depth: int = 2):
+    """Pipelined inference over a sequence of CPU batches: yields
+    ``model(to_device(x)).cpu()`` for each batch ``x`` of ``batches``, in
+    order.
+
+    Whole batches travel on three streams: batch k+1 uploads (upload stream)
+    while batch k computes (runtime stream) and batch k-1 reads back
+    (readback stream), so a stream of batches pays one upload and one readback
+    of latency in all, not per batch, and each forward runs at the full batch
+    size.  Up to ``depth`` batches beyond the one being returned stay in
+    flight, so the upload of a batch is enqueued well before the forward of the
+    batch ahead of it ends (with depth 1 it would wait for the previous
+    readback).  Batches should be in page-locked memory (``matrixman.pinned_empty``)
+    for the copies to be asynchronous.  ``model`` is a prepared module with one
+    batch-major tensor output.  Each yielded result is a CPU tensor (pooled
+    page-locked memory when available) that stays valid after the next batch
+    is submitted."""
+    from .api import _device_index, get_backend
+
+    if int(depth) < 1:
+        raise ValueError("MatrixMan: infer_stream depth must be at least 1")
+    get_backend()
+    rt = runtime.get_runtime(_device_index(device))
+    runtime.set_device(rt.index)
+    lib = _lib.load()
+    up, down = _streams(rt)
+    safe_reuse = runtime.config.resolved_sync_policy == "safe"
+    pending = []  # (event after readback, host output, device blocks kept alive)
+    events = []
+    # Input blocks: a ring of depth + 1 per input size, each reused only after
+    # the forward that read it (its `consumed` event).  A block freed to the
+    # arena would carry a release event at the tail of the runtime stream --
+    # after the forward just submitted -- and the next upload into it could not
+    # overlap that forward.
+    rings: dict[int, list] = {}
+    uses: dict[int, int] = {}
+
+    def _event(track=True):
+        h = ctypes.c_void_p()
+        _lib.check(lib.mm_event_create(ctypes.byref(h), 0), "event create")
+        if track:
+            events.append(h)
+        return h
+
+    def _finish(item):
+        done, out, _keep, evs = item
+        _lib.check(lib.mm_event_sync(done, runtime.config.waitTimeoutMs), "readback wait")
+        for h in evs:  # this batch's events are no longer waited on
+            lib.mm_event_destroy(h)
+        return out
+
+    try:
+        with torch.no_grad():
+            for x in batches:
+                if not isinstance(x, torch.Tensor) or x.device.type != "cpu" or x.dtype != torch.float32:
+                    raise TypeError("MatrixMan: infer_stream expects float32 CPU batches")
+                if x.dim() < 1 or x.shape[0] == 0:
+                    raise ValueError("MatrixMan: infer_stream needs non-empty batches")
+                x = x.contiguous()
+                n = int(x.shape[0])
+                row = x[0].numel()
+                shape = (n,) + tuple(int(v) for v in x.shape[1:])
+                uploaded, computed, done = _event(False), _event(False), _event(False)
+                ring = rings.setdefault(n * row, [])
+                use = uses.get(n * row, 0)
+                uses[n * row] = use + 1
+                if len(ring) <= int(depth):
+                    if safe_reuse:
+                        # Ordered on the upload stream: a block reused from the
+                        # arena makes it wait for that block's release only.
+                        storage = rt.new_storage(n * row, torch.float32, stream=up)
+                    else:
+                        # Stream-ordered reuse only: the upload waits for the
+                        # point of the runtime stream where it was allocated.
+                        storage = rt.new_storage(n * row, torch.float32)
+                        allocated = _event()
+                        _lib.check(lib.mm_event_record(allocated, rt.stream), "event record")
+                        _lib.check(lib.mm_stream_wait_event(up, allocated), "stream wait")
+                    ring.append((storage, _event()))
+                storage, consumed = ring[use % len(ring)]
+                if use >= len(ring):
+                    _lib.check(lib.mm_stream_wait_event(up, consumed), "stream wait")
+                _lib.check(lib.mm_memcpy_h2d(ctypes.c_void_p(storage.pointer), ctypes.c_void_p(x.data_ptr()),
+                                             n * row * 4, up, 0), "host-to-device copy")
+                _lib.check(lib.mm_event_record(uploaded, up), "event record")
+                _lib.check(lib.mm_stream_wait_event(rt.stream, uploaded), "stream wait")
+                xd = MatrixManTensor._from_owner(storage, shape, 0, contiguous_strides(shape))
+                y = model(xd)
+                if not isinstance(y, MatrixManTensor):
+                    raise NotImplementedError("MatrixMan: infer_stream needs a model with one tensor output")
+                if tuple(y._logical_strides) != contiguous_strides(tuple(int(v) for v in y.shape)):
+                    from . import ops
+                    y = ops.materialize(y)
+                out = runtime.host_empty((n,) + tuple(int(v) for v in y.shape[1:]), torch.float32)
+                _lib.check(lib.mm_event_record(consumed, rt.stream), "event record")
+                _lib.check(lib.mm_event_record(computed, rt.stream), "event record")
+                _lib.check(lib.mm_stream_wait_event(down, computed), "stream wait")
+                _lib.check(lib.mm_memcpy_d2h(ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(y.element_ptr),
+                                             out.numel() * 4, down, 0), "device-to-host copy")
+                _lib.check(lib.mm_event_record(done, down), "event record")
+                # The input and output blocks go back to the arena only after
+                # their readback (the host waits for `done` first).
+                pending.append((done, out, (xd, y), (uploaded, computed, done)))
+                if len(pending) > int(depth):
+                    yield _finish(pending.pop(0))
+            while pending:
+                yield _finish(pending.pop(0))
+    finally:
+        try:
+            lib.mm_stream_sync(ctypes.c_void_p(down), runtime.config.waitTimeoutMs)
+            lib.mm_stream_sync(ctypes.c_void_p(up), runtime.config.waitTimeoutMs)
+        finally:
+            for item in pending:
+                for h in item[3]:
+                    lib.mm_event_destroy(h)
+            pending.clear()
+            rt.synchronize()  # the ring's blocks may return to the arena now
+            rings.clear()
+            for h in events:
+                lib.mm_event_destroy(h)

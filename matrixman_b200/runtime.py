@@ -190,9 +190,13 @@ class DeviceRuntime:
         self.launch_count = 0
 
     # -- memory ----------------------------------------------------------
-    def alloc(self, nbytes: int, kind: int = _lib.POOL_ACTIVATION) -> int:
+    def alloc(self, nbytes: int, kind: int = _lib.POOL_ACTIVATION, stream=None) -> int:
+        """Arena block ordered on ``stream`` (default: the runtime stream);
+        under the safe sync policy a reused block makes that stream wait for
+        the block's release event."""
         out = ctypes.c_void_p()
-        _lib.check(self.lib.mm_alloc(self.index, max(int(nbytes), 1), kind, self.stream,
+        _lib.check(self.lib.mm_alloc(self.index, max(int(nbytes), 1), kind,
+                                     self.stream if stream is None else stream,
                                      ctypes.byref(out)), "allocate")
         return int(out.value)
 
@@ -200,9 +204,9 @@ class DeviceRuntime:
         _lib.check(self.lib.mm_free(ctypes.c_void_p(pointer), self.stream), "free")
 
     def new_storage(self, numel: int, dtype: torch.dtype = torch.float32,
-                    kind: int = _lib.POOL_ACTIVATION) -> DeviceStorage:
+                    kind: int = _lib.POOL_ACTIVATION, stream=None) -> DeviceStorage:
         nbytes = max(int(numel), 1) * ELEMENT_SIZE[dtype]
-        return DeviceStorage(self, self.alloc(nbytes, kind), nbytes, dtype, kind)
+        return DeviceStorage(self, self.alloc(nbytes, kind, stream), nbytes, dtype, kind)
 
     def pool_stats(self) -> dict:
         st = _lib.MMPoolStats()

@@ -165,3 +165,25 @@ def test_infer_explicit_sizes(mm):
         for bad in ([3, 3], [7, 0], [8, -1], []):
             with pytest.raises(ValueError):
                 mm.infer(prepared, x, sizes=bad)
+
+
+@pytest.mark.parametrize("depth", [1, 2, 3])
+def test_infer_stream_matches_serial(mm, depth):
+    """The streaming API yields, in order, exactly the serial results of each
+    batch (batches of different sizes and contents, several in flight)."""
+    model = W.yolov8_model("n")
+    prepared = mm.prepare(model)
+    batches = []
+    for i, n in enumerate((3, 3, 1, 4, 3)):
+        x = mm.pinned_empty((n, 3, 256, 256))
+        x.copy_(W.yolo_input(n, seed=70 + i, size=256))
+        batches.append(x)
+    with torch.no_grad():
+        refs = [prepared(mm.to_device(x)).cpu() for x in batches]
+        outs = [y.clone() for y in mm.infer_stream(prepared, batches, depth=depth)]
+    assert len(outs) == len(refs)
+    for y, ref in zip(outs, refs):
+        assert y.shape == ref.shape
+        assert torch.equal(y, ref)
+    with pytest.raises(ValueError):
+        list(mm.infer_stream(prepared, batches, depth=0))

@@ -73,6 +73,9 @@ def test_config1_conv(mm):
     (12, 24, 5, 1, 2, 1, 3, 11, 2),
     (3, 64, 7, 2, 3, 1, 1, 56, 1),
     (3, 20, 3, 2, 1, 1, 1, 31, 1),   # stem with a partial second 16-channel group
+    (4, 16, 3, 1, 1, 1, 1, 70, 2),   # stride-1 stem, partial tiles
+    (1, 8, 3, 2, 0, 1, 1, 67, 1),    # one channel, no padding
+    (2, 32, 3, 1, 0, 1, 1, 9, 3),    # tiny images, two channel groups
 ])
 def test_conv_shapes_nchw_and_nhwc(mm, c, k, ksz, stride, pad, dil, groups, hw, n):
     g = gen(c * 100 + k)
