@@ -38,13 +38,57 @@ NC = 80
 ANCHORS = (IMAGE // 8) ** 2 + (IMAGE // 16) ** 2 + (IMAGE // 32) ** 2
 
 
+class Spec:
+    """One benchmark configuration: model, seeded synthetic input, batch per
+    GPU (weak scaling) or in total (strong scaling), and the CPU sample the
+    ground-truth timing runs on."""
+
+    def __init__(self, key, metric, unit, model, inputs, batch, scaling, desc, cpu_sample):
+        self.key, self.metric, self.unit = key, metric, unit
+        self.model, self.inputs = model, inputs
+        self.batch, self.scaling, self.desc, self.cpu_sample = batch, scaling, desc, cpu_sample
+
+    def batch_per_gpu(self, world: int, override=None) -> int:
+        b = int(override) if override else self.batch
+        if self.scaling == "strong":
+            if b % world:
+                raise SystemExit(f"bench: total batch {b} does not split over {world} GPUs")
+            return b // world
+        return b
+
+
+def _specs():
+    import workloads as W
+    return {
+        "y8n": Spec("y8n", METRIC, UNIT, lambda: W.yolov8_model("n"),
+                    lambda b, s: W.yolo_input(b, seed=s), BATCH, "weak",
+                    "yolov8n 640x640 fp32 inference", 8),
+        "y8n1": Spec("y8n1", METRIC, UNIT, lambda: W.yolov8_model("n"),
+                     lambda b, s: W.yolo_input(b, seed=s), 1, "weak",
+                     "yolov8n 640x640 fp32 inference", 4),
+        "y8m": Spec("y8m", "YOLOv8m 640x640 fp32 images/sec", UNIT, lambda: W.yolov8_model("m"),
+                    lambda b, s: W.yolo_input(b, seed=s), 256, "strong",
+                    "yolov8m 640x640 fp32 inference, a batch of 256 split over the GPUs", 2),
+        "r18": Spec("r18", "ResNet-18 224x224 fp32 images/sec", UNIT, W.resnet18_model,
+                    lambda b, s: W.resnet18_input(b, seed=s), 32, "weak",
+                    "resnet18 224x224 fp32 eval inference (softmax head)", 16),
+        "mlp": Spec("mlp", "MLP 784-512-256-10 fp32 samples/sec", "samples/s", W.mlp_model,
+                    lambda b, s: W.mlp_input(b, seed=s), 256, "weak",
+                    "MLP 784-512-256-10 (ReLU) + softmax fp32", 256),
+    }
+
+
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--batch", type=int, default=BATCH)
+    p.add_argument("--workload", choices=("y8n", "y8n1", "y8m", "r18", "mlp", "c1"), default="y8n",
+                   help="y8n: YOLOv8n bs64 (the headline); y8n1: YOLOv8n bs1; y8m: YOLOv8m, 256 "
+                        "images split over the GPUs; r18: ResNet-18 bs32; mlp: MLP bs256; "
+                        "c1: the single [1,4,320,320] x [5,4,3,3] convolution")
+    p.add_argument("--batch", type=int, default=None, help="batch per GPU (total for y8m)")
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--e2e-chunks", type=int, default=4,
                    help="1 GPU: matrixman.infer chunks (upload / forward / readback overlap)")
@@ -156,14 +200,14 @@ def profile_launches(matrixman, prepared, x_dev) -> dict:
     return summary
 
 
-def cpu_baseline(model, batch_sample: int, min_seconds: float = 12.0) -> dict:
+def cpu_baseline(model, batch_sample: int, spec=None, min_seconds: float = 12.0) -> dict:
     """Stock PyTorch CPU fp32 on this host's cores (the reference's ground truth)."""
     import torch
-    import workloads as W
     from oracle.models import cpu_model_name
+    spec = spec or _specs()["y8n"]
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    x = W.yolo_input(batch_sample, seed=99)
+    x = spec.inputs(batch_sample, 99)
     with torch.no_grad():
         model(x)  # warm-up
         n, t0 = 0, time.perf_counter()
@@ -173,24 +217,24 @@ def cpu_baseline(model, batch_sample: int, min_seconds: float = 12.0) -> dict:
             el = time.perf_counter() - t0
             if el >= min_seconds or n >= 200:
                 break
-    return {"value": n * batch_sample / el, "unit": UNIT, "cores": torch.get_num_threads(),
+    return {"value": n * batch_sample / el, "unit": spec.unit, "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"{n} forwards of an unprepared YOLOv8n bs{batch_sample} 640x640 on torch CPU "
-                      f"fp32 ({cpu_model_name()}, {threads} threads), {el:.1f} s"}
+            "sample": f"{n} forwards of the unprepared model ({spec.desc}) at batch {batch_sample} "
+                      f"on torch CPU fp32 ({cpu_model_name()}, {threads} threads), {el:.1f} s"}
 
 
-def output_parity(model, out_cpu, batch: int, world: int, images: int = 2) -> dict:
+def output_parity(model, out_cpu, batch: int, world: int, images: int = 2, spec=None) -> dict:
     """Checker (outside every timed region): the first `images` images of each
     rank's slice of the timed step's output against the CPU ground truth (the
     unprepared model on torch CPU fp32, the same computation the CPU baseline
     times), as max |diff| / max |ref| -- the parity bar is 1e-4."""
-    import torch
-    import workloads as W
     from oracle.models import run_cpu
     from oracle.tolerance import CONV_GEMM_REL, max_rel_err
+    spec = spec or _specs()["y8n"]
     worst = 0.0
+    images = min(images, batch)
     for r in range(world):
-        x = W.yolo_input(batch, seed=1000 + r)[:images]
+        x = spec.inputs(batch, 1000 + r)[:images]
         ref = run_cpu(model, x)
         got = out_cpu[r * batch:r * batch + images]
         worst = max(worst, max_rel_err(got, ref))
@@ -202,7 +246,7 @@ def output_parity(model, out_cpu, batch: int, world: int, images: int = 2) -> di
                     + " vs the unprepared model on torch CPU fp32"}
 
 
-def run_b200(args):
+def run_b200(args, spec):
     import torch
     import torch.distributed as dist
 
@@ -223,16 +267,17 @@ def run_b200(args):
     from matrixman_b200 import runtime
     from matrixman_b200 import telemetry as profiling
     from matrixman_b200.replicas import PeerGather
-    from workloads.yolov8 import macs_per_image
 
     runtime.set_device(local)
     matrixman.init()
     rt = runtime.get_runtime(local)
-    batch = args.batch
-    model = W.yolov8_model("n")
+    batch = spec.batch_per_gpu(world, args.batch)
+    model = spec.model()
     prepared = matrixman.prepare(model)
-    x_host = W.yolo_input(batch, seed=1000 + rank)
+    x_host = spec.inputs(batch, 1000 + rank)
     x_dev = matrixman.to_device(x_host, device=local)
+    with torch.no_grad():
+        out_tail = tuple(int(v) for v in prepared(x_dev).shape[1:])
 
     def barrier():
         # an all-reduce of an explicit CUDA tensor (dist.barrier would place its
@@ -248,11 +293,12 @@ def run_b200(args):
     if world > 1:
         # Rank 0's gather buffers, written by every rank's copy engines over
         # NVLink (CUDA IPC); the copies of one step overlap the next forward.
-        gather = PeerGather((4 + NC, ANCHORS), sizes, device=local)
+        gather = PeerGather(out_tail, sizes, device=local)
 
     def step(xd):
         """One step: the replica's forward; with several ranks, plus the
-        copy of this rank's [B, 84, 8400] output into rank 0's gather buffer."""
+        copy of this rank's output (e.g. [B, 84, 8400]) into rank 0's gather
+        buffer."""
         y = prepared(xd)
         if gather is not None:
             gather.push(y)
@@ -331,9 +377,11 @@ def run_b200(args):
         e2e_s = float(t.item())
     checked = full.cpu() if (rank == 0 and full is not None and not args.no_parity) else None
     del full
-    parity = output_parity(model, checked, batch, world) if checked is not None else None
-    out_numel = batch * (4 + NC) * ANCHORS * world
-    e2e = {"value": world * batch / e2e_s, "unit": UNIT,
+    parity = output_parity(model, checked, batch, world, spec=spec) if checked is not None else None
+    out_numel = batch * world
+    for v in out_tail:
+        out_numel *= v
+    e2e = {"value": world * batch / e2e_s, "unit": spec.unit,
            "h2d_bytes_per_step": int(x_host.numel() * 4) * world,
            "d2h_bytes_per_step": int(out_numel * 4), "ms_per_step": e2e_s * 1e3, "steps": e2e_steps,
            "api": f"matrixman.infer_stream(prepared, {e2e_steps} pinned batches of {batch})"
@@ -342,12 +390,12 @@ def run_b200(args):
                            "api": f"matrixman.infer(prepared, pinned batch, chunks={args.e2e_chunks})"}}
     return {"world": world, "rank": rank, "local": local, "value": value, "ms_step": ms_step,
             "clocks": clock_info, "e2e": e2e, "launch_calls": launch_calls, "prepared": prepared,
-            "x_dev": x_dev, "model": model, "macs": macs_per_image(model), "batch": batch,
+            "x_dev": x_dev, "model": model, "macs": W.macs_per_sample(model, x_host[:1]), "batch": batch,
             "parity": parity, "gather": gather,
             "matrixman": matrixman, "dist": dist if world > 1 else None}
 
 
-CONV_ENTRIES = ("mm_conv2d", "mm_conv2d_tc")
+CONV_ENTRIES = ("mm_conv2d", "mm_conv2d_tc", "mm_gemm")
 TRAFFIC_SUMMARY = ROOT / "profiles" / "conv_tc_yolov8n_bs64_traffic.md"
 
 
@@ -367,7 +415,7 @@ def conv_traffic_per_launch():
     return None
 
 
-def roofline(res: dict) -> tuple[dict, int, dict]:
+def roofline(res: dict, spec=None) -> tuple[dict, int, dict]:
     """Dominant kernel family (convolution) from one event-timed eager forward.
 
     achieved = algorithmic conv FLOPs of one forward (2 * MACs * batch) / the
@@ -389,7 +437,8 @@ def roofline(res: dict) -> tuple[dict, int, dict]:
     peak = peaks["bf16_tflops_sustained"]
     ceiling = peak / 6.0
     kernels_per_forward = sum(v["launches"] for v in summary.values())
-    traffic = conv_traffic_per_launch()
+    # (the committed DRAM-traffic capture covers the YOLOv8n batch-64 forward)
+    traffic = conv_traffic_per_launch() if spec is None or spec.key == "y8n" else None
     roof = {"bound": "tensor", "kernel": "+".join(k for k in CONV_ENTRIES if k in summary),
             "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4) if peak else None,
@@ -416,27 +465,36 @@ def main():
         return run_profile_case(args)
     if args.profile_conv:
         return run_profile_conv(args)
-    res = run_b200(args)
-    roof, kernels_per_forward, shares = roofline(res)
+    if args.workload == "c1":
+        return run_c1(args)
+    spec = _specs()[args.workload]
+    res = run_b200(args, spec)
+    roof, kernels_per_forward, shares = roofline(res, spec)
+    in_bytes = res["batch"] * res["x_dev"].numel() // max(int(res["x_dev"].shape[0]), 1) * 4
     line = {
-        "metric": METRIC, "value": round(res["value"], 2), "unit": UNIT, "n_gpus": res["world"],
+        "metric": spec.metric, "value": round(res["value"], 2), "unit": spec.unit, "n_gpus": res["world"],
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(res["ms_step"], 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic U[0,1] images, random-init weights (seeded)",
-        "config": {"workload": f"yolov8n 640x640 fp32 inference, {res['batch']} images per GPU, "
+        "higher_is_better": True, "scaling": spec.scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic seeded inputs (shapes and distributions of the configuration), "
+                "random-init weights (seeded)",
+        "config": {"workload": f"{spec.desc}, {res['batch']} per GPU, "
                                "prepared (BN folded, NHWC, CUDA graph)"
                                + (", every step's outputs gathered in rank 0's HBM by copy-engine "
                                   "writes over NVLink (CUDA IPC), overlapped with the next forward"
                                   if res["world"] > 1 else ""),
                    "batch_per_gpu": res["batch"], "global_batch": res["batch"] * res["world"],
-                   "image": [IMAGE, IMAGE], "parallelism": f"replicas{res['world']}",
-                   "l2": "inputs larger than L2 (315 MB input per step per GPU)"},
+                   "parallelism": f"replicas{res['world']}",
+                   "l2": (f"inputs larger than L2 ({in_bytes / 1e6:.0f} MB input per step per GPU)"
+                          if in_bytes > 126e6 else
+                          f"{in_bytes / 1e6:.1f} MB input per step, L2-resident (latency-bound config)")},
         "e2e": res["e2e"], "roofline": roof, "parity": res["parity"],
         "gpu_launches": kernels_per_forward * args.steps, "clocks": res["clocks"],
         "kernel_shares": shares,
     }
+    if spec.key in ("y8n", "y8n1", "y8m"):
+        line["config"]["image"] = [IMAGE, IMAGE]
     if res["world"] == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(res["model"], 8)
+        line["cpu_baseline"] = cpu_baseline(res["model"], min(spec.cpu_sample, res["batch"] * 64), spec)
     if res["dist"] is not None:
         import torch
         if res["gather"] is not None:
@@ -490,39 +548,169 @@ def run_profile_conv(args):
 
 
 def run_reference(args, world, rank):
-    """Reference arm: the path's CPU ground truth (unprepared model, torch CPU fp32)."""
+    """Reference arm: the path's CPU ground truth (the unprepared model on
+    torch CPU fp32, or the single convolution for c1), rank 0 only."""
     if rank != 0:
         return
     import torch
+    import torch.nn.functional as F
     import workloads as W
     from oracle.models import cpu_model_name
-    model = W.yolov8_model("n")
-    sample = 8
-    x = W.yolo_input(sample, seed=99)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     steps = max(1, min(args.steps, 5))
-    with torch.no_grad():
-        for _ in range(max(1, min(args.warmup, 1))):
+    if args.workload == "c1":
+        x, w = W.conv1_case(0)
+        reps = 200  # convolutions per step (about a second of CPU work)
+        with torch.no_grad():
+            F.conv2d(x, w, None, 1, 1)
+            t0 = time.perf_counter()
+            for _ in range(steps * reps):
+                F.conv2d(x, w, None, 1, 1)
+            el = time.perf_counter() - t0
+        value, unit, metric = steps * reps / el, "convs/s", C1_METRIC
+        workload = "conv2d [1,4,320,320] x [5,4,3,3] s1 p1 fp32 on torch CPU, " \
+                   f"{reps} convolutions per step"
+        sample = f"{steps * reps} convolutions on {cpu_model_name()}"
+        ms = el / steps * 1e3
+    else:
+        spec = _specs()[args.workload]
+        model = spec.model()
+        n = min(spec.cpu_sample, spec.batch_per_gpu(1, args.batch))
+        x = spec.inputs(n, 99)
+        with torch.no_grad():
             model(x)
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            model(x)
-        el = time.perf_counter() - t0
-    value = steps * sample / el
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                model(x)
+            el = time.perf_counter() - t0
+        value, unit, metric = steps * n / el, spec.unit, spec.metric
+        workload = f"{spec.desc} (unprepared, torch CPU fp32), bounded sample of {n} per step"
+        sample = f"{steps} x batch-{n} forwards on {cpu_model_name()}"
+        ms = el / steps * 1e3
     line = {
-        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": steps,
-        "warmup": 1, "ms_per_step": round(el / steps * 1e3, 2), "higher_is_better": True,
+        "metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": steps,
+        "warmup": 1, "ms_per_step": round(ms, 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
-        "data": "synthetic U[0,1] images, random-init weights (seeded)",
-        "config": {"workload": "yolov8n 640x640 fp32 inference (unprepared, torch CPU fp32), "
-                               f"bounded sample of {sample} images per step",
-                   "batch_per_gpu": BATCH, "image": [IMAGE, IMAGE], "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": torch.get_num_threads(),
-                         "kind": "port",
-                         "sample": f"{steps} x bs{sample} forwards on {cpu_model_name()}"},
-        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "data": "synthetic seeded inputs, random-init weights (seeded)",
+        "config": {"workload": workload, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    print(json.dumps(line), flush=True)
+
+
+C1_METRIC = "conv2d [1,4,320,320]x[5,4,3,3] s1 p1 fp32 convolutions/sec"
+C1_BYTES = 4 * (1 * 4 * 320 * 320 + 1 * 5 * 320 * 320 + 5 * 4 * 3 * 3)  # 3,687,120 B minimal traffic
+
+
+def run_c1(args):
+    """Config 1: the reference's conv demo shape, one convolution per step.
+
+    HBM-bound (3,687,120 algorithmic bytes) and launch-latency-bound.  The
+    working set of one call (3.7 MB) fits in L2, so the timed steps rotate
+    over 48 distinct input/output pairs (177 MB, more than the 126 MB L2).
+    value: convolutions/s over K device-timed steps; e2e: the public API
+    (to_device of a pinned input, F.conv2d with the CPU weight, .cpu())."""
+    import torch
+    import torch.nn.functional as F
+
+    import matrixman_b200 as matrixman
+    import workloads as W
+    from matrixman_b200 import ops, runtime
+    from matrixman_b200 import telemetry as profiling
+    from oracle import ops as O
+    from oracle.models import cpu_model_name
+    from oracle.tolerance import CONV_GEMM_REL, max_rel_err
+
+    world, rank, local = dist_env()
+    if world > 1:
+        raise SystemExit("bench: the c1 workload is a single-GPU configuration")
+    matrixman.init()
+    rt = runtime.get_runtime(local)
+    x, w = W.conv1_case(0)
+    ring = 48
+    xs = [matrixman.to_device(x * (1.0 + 0.01 * i), device=local) for i in range(ring)]
+    wd = matrixman.to_device(w, device=local)
+    ys = [ops.empty(rt, (1, 5, 320, 320)) for _ in range(ring)]
+
+    def conv(i):
+        ops.convolution(xs[i], wd, None, (1, 1), (1, 1), (1, 1), 1, out=ys[i])
+
+    for i in range(max(args.warmup, 3) * ring):
+        conv(i % ring)
+    rt.synchronize()
+    steps = max(args.steps, ring)
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_pre = time.perf_counter()
+    while time.perf_counter() - t_pre < 0.4:
+        conv(0)
+        rt.synchronize()
+    launches0 = profiling.total_launches()
+    timer = runtime.Timer(rt)
+    timer.start()
+    for i in range(steps):
+        conv(i % ring)
+    timer.stop()
+    ms_total = timer.elapsed_ms()
+    launches = profiling.total_launches() - launches0
+    clock_info = clocks.stop()
+    ms = ms_total / steps
+    value = 1e3 / ms
+    peaks = measured_peaks()
+    achieved = C1_BYTES / (ms / 1e3) / 1e9
+    y_last = ys[(steps - 1) % ring].cpu()
+    ref = O.conv2d(x * (1.0 + 0.01 * ((steps - 1) % ring)), w, None, 1, 1)
+    err = max_rel_err(y_last, ref)
+    # End to end through the public API.
+    xp = matrixman.pinned_empty(x.shape)
+    xp.copy_(x)
+    with torch.no_grad():
+        for _ in range(5):
+            F.conv2d(matrixman.to_device(xp, device=local), w, None, 1, 1).cpu()
+        t0 = time.perf_counter()
+        n_e2e = 200
+        for _ in range(n_e2e):
+            F.conv2d(matrixman.to_device(xp, device=local), w, None, 1, 1).cpu()
+        e2e_s = (time.perf_counter() - t0) / n_e2e
+    line = {
+        "metric": C1_METRIC, "value": round(value, 1), "unit": "convs/s", "n_gpus": 1, "steps": steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "x ~ U[-1,1] seeded, Kaiming-uniform weight (the reference's conv demo case)",
+        "config": {"workload": "conv2d [1,4,320,320] x [5,4,3,3] s1 p1, no bias (config 1)",
+                   "l2": f"timed steps rotate over {ring} input/output pairs "
+                         f"({ring * C1_BYTES / 1e6:.0f} MB > 126 MB L2)",
+                   "parallelism": "single GPU"},
+        "e2e": {"value": round(1.0 / e2e_s, 1), "unit": "convs/s", "h2d_bytes_per_step": int(x.numel() * 4),
+                "d2h_bytes_per_step": int(5 * 320 * 320 * 4), "ms_per_step": e2e_s * 1e3,
+                "api": "F.conv2d(matrixman.to_device(pinned x), cpu weight).cpu()"},
+        "roofline": {"bound": "hbm", "kernel": "mm_conv2d (direct small-channel kernel)",
+                     "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "algorithmic_bytes_per_launch": C1_BYTES,
+                     "peak_basis": f"{peaks['source']} HBM copy bandwidth",
+                     "note": "one 3.7 MB convolution per launch: launch latency, not bandwidth, "
+                             "bounds a single call"},
+        "parity": {"max_rel_err": err, "bar": CONV_GEMM_REL, "ok": bool(err < CONV_GEMM_REL),
+                   "what": "last timed step's output vs torch CPU conv2d"},
+        "gpu_launches": launches, "clocks": clock_info,
+    }
+    if not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        with torch.no_grad():
+            F.conv2d(x, w, None, 1, 1)
+            t0 = time.perf_counter()
+            n = 0
+            while time.perf_counter() - t0 < 10.0:
+                F.conv2d(x, w, None, 1, 1)
+                n += 1
+            el = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(n / el, 1), "unit": "convs/s", "cores": torch.get_num_threads(),
+                                "kind": "port",
+                                "sample": f"{n} convolutions on torch CPU fp32 ({cpu_model_name()}), {el:.1f} s"}
     print(json.dumps(line), flush=True)
 
 

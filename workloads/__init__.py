@@ -110,3 +110,31 @@ def yolov8_model(variant: str = "n", seed: int = 3, nc: int = 80) -> nn.Module:
 
 def yolo_input(batch: int = 1, seed: int = 13, size: int = 640) -> torch.Tensor:
     return torch.rand(batch, 3, size, size, generator=_gen(seed))
+
+
+def macs_per_sample(model: nn.Module, sample: torch.Tensor) -> int:
+    """Multiply-accumulates of every Conv2d and Linear for one input sample
+    (a batch-1 CPU tensor), counted with forward hooks (the YOLOv8 DFL's fixed
+    1x1 convolution excluded, as in ``yolov8.macs_per_image``)."""
+    from .yolov8 import DFL
+    total = 0
+    hooks = []
+    dfl_convs = {id(m.conv) for m in model.modules() if isinstance(m, DFL)}
+
+    def hook(mod, inp, out):
+        nonlocal total
+        if id(mod) in dfl_convs:
+            return
+        if isinstance(mod, nn.Conv2d):
+            k = mod.kernel_size[0] * mod.kernel_size[1] * (mod.in_channels // mod.groups)
+            total += out.numel() // out.shape[0] * k
+        elif isinstance(mod, nn.Linear):
+            total += out.numel() // out.shape[0] * mod.in_features
+    for m in model.modules():
+        if isinstance(m, (nn.Conv2d, nn.Linear)):
+            hooks.append(m.register_forward_hook(hook))
+    with torch.no_grad():
+        model(sample)
+    for hk in hooks:
+        hk.remove()
+    return total
