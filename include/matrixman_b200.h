@@ -400,6 +400,15 @@ int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float* w_lo, int
  * frees its tensor memory and returns, and the host reads the code here. */
 int mm_kernel_error(int device, int* code_out, int clear);
 
+/* Test hook for the bounded-wait error path of mm_conv2d_tc (no counterpart in
+ * the reference): for later launches on `device`, the budget of every
+ * device-side wait (wait_ns <= 0 restores the default 200 ms) and, when
+ * drop_first_load != 0, CTA 0 leaves its first k-block's loads unissued so that
+ * the waits for that stage run out: the kernel records an error code (read
+ * with mm_kernel_error), finishes its own in-flight copies and MMAs, frees its
+ * tensor memory and returns.  Not for production use. */
+int mm_debug_tc_fault(int device, int64_t wait_ns, int drop_first_load);
+
 /* Split prepacked weights into the tf32 high part and the fp32 remainder
  * (w_hi = w with its 13 low mantissa bits cleared, w_lo = w - w_hi), in place on
  * the device: n elements of src -> hi, lo. */

@@ -180,6 +180,7 @@ SIGNATURES = {
     "mm_ipc_open": [_i, _vp, ctypes.POINTER(ctypes.c_void_p)],
     "mm_ipc_close": [_i, _vp],
     "mm_kernel_error": [_i, ctypes.POINTER(_i), _i],
+    "mm_debug_tc_fault": [_i, _i64, _i],
     "mm_gemm": [_T, _T, _T, _d, _d, _i, _T, _vp],
     "mm_yolo_decode": [_TT, ctypes.POINTER(ctypes.c_float), _i, _i, _i, _T, _vp],
     "mm_detect_reduce": [_T, _T, _vp],

@@ -70,7 +70,7 @@ constexpr int TC_BK = 32;         // channels per k-block (128 bytes of fp32)
 constexpr uint32_t TC_SPIN_LIMIT = 1u << 26;
 
 enum TcError { TC_ERR_NONE = 0, TC_ERR_WAIT_A = 1, TC_ERR_WAIT_B = 2, TC_ERR_WAIT_EMPTY = 3,
-               TC_ERR_WAIT_ACC = 4 };
+               TC_ERR_WAIT_ACC = 4, TC_ERR_DRAIN = 5 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -129,10 +129,15 @@ __device__ __forceinline__ bool tc_error_raised() {
   return *reinterpret_cast<volatile int*>(&g_tc_error) != 0;
 }
 
-// Bounded wait; returns false (and records `code`) after TC_WAIT_NS, or at
-// once when another CTA has already recorded an error, so a stuck pipeline
-// ends the whole grid within a fraction of a second.
+// Bounded wait; returns false (and records `code`) after g_tc_wait_ns
+// (200 ms unless a test shortened it with mm_debug_tc_fault), or soon after
+// another CTA has recorded an error, so a stuck pipeline ends the whole grid
+// within a fraction of a second.
 constexpr uint64_t TC_WAIT_NS = 200ull * 1000 * 1000;
+__device__ unsigned long long g_tc_wait_ns = TC_WAIT_NS;
+// Test hook (mm_debug_tc_fault): CTA 0 issues nothing for its first k-block,
+// so a wait for that stage runs out and the error path runs.
+__device__ int g_tc_drop_first_load = 0;
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -141,10 +146,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
     if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
     if ((i & 63) == 0) {
       if (tc_error_raised()) return false;
-      if (global_ns() - t0 > TC_WAIT_NS) break;
+      if (global_ns() - t0 > *reinterpret_cast<volatile unsigned long long*>(&g_tc_wait_ns)) break;
     }
   }
   atomicCAS(&g_tc_error, 0, code);
+  return false;
+}
+
+// Wait for this CTA's own asynchronous work (bulk copies in flight, MMAs
+// committed) on the error path: it ignores the error flag -- no bulk copy may
+// land in shared memory after the CTA exits, and no MMA may write TMEM after
+// it is freed -- and gives up only after TC_WAIT_NS (recording TC_ERR_DRAIN).
+__device__ __forceinline__ bool mbar_drain_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1; i < TC_SPIN_LIMIT; ++i) {
+    if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+    if ((i & 63) == 0 && global_ns() - t0 > TC_WAIT_NS) break;
+  }
+  atomicCAS(&g_tc_error, 0, (int)TC_ERR_DRAIN);
   return false;
 }
 
@@ -649,7 +669,7 @@ __device__ __forceinline__ void tc_issue(const TcArgs& a, uint8_t* smem, const T
     // Error path: no MMA of this warp may still write TMEM when it is freed.
     if (elect_one()) mma_commit(&B.drain[ROLE]);
     __syncwarp();
-    mbar_wait(&B.drain[ROLE], 0u, TC_ERR_WAIT_ACC);
+    mbar_drain_wait(&B.drain[ROLE], 0u);
   }
 }
 
@@ -1064,6 +1084,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int st = 0;
       uint32_t par = 0;
       bool alive = true;
+      // Test hook (mm_debug_tc_fault): CTA 0 issues nothing for its first
+      // k-block, so the waits for that stage run out.
+      const bool dropped = blockIdx.x == 0 && *reinterpret_cast<volatile int*>(&g_tc_drop_first_load) != 0;
       for (int64_t tile = blockIdx.x; tile < a.tiles && alive; tile += gridDim.x) {
         const TcTile t = tc_tile(a, (int)(tile / a.n_tiles));
         const int n0 = (int)(tile % a.n_tiles) * a.bn;
@@ -1074,7 +1097,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             break;
           }
           const int nsub = min(KS, a.sb_total - kb * KS);
-          if (elect_one()) {
+          if (!(dropped && g == 0) && elect_one()) {
             uint8_t* stage = smem + (size_t)st * L.stage_bytes;
             // TMA modes: A and both weight tiles complete on full_x; gather
             // mode: the weights on full_b (A arrives by the producers' cp.async).
@@ -1126,11 +1149,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       // Bulk copies must not outlive the CTA's shared memory.
       for (int64_t k = (g > S ? g - S : 0); k < g; ++k) {
+        if (k == 0 && dropped) continue;  // (nothing was issued for it)
         const uint32_t kp = (uint32_t)((k / S) & 1);
         if (a.amode == TC_A_GATHER)
-          mbar_wait(&full_b[k % S], kp, TC_ERR_WAIT_B);
+          mbar_drain_wait(&full_b[k % S], kp);
         else
-          mbar_wait(&full_x[k % S], kp, TC_ERR_WAIT_A);
+          mbar_drain_wait(&full_x[k % S], kp);
       }
     }
   } else if (warp == TC_WARP_HI) {
@@ -1703,6 +1727,23 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
                      amap, ymap, a),
           "mm_conv2d_tc launch");
   MM_LAUNCH_CHECK("mm_conv2d_tc launch");
+  return MM_OK;
+}
+
+// Test hook for the bounded-wait error path (no counterpart in the
+// reference): sets the budget of the kernel's waits on `device` (wait_ns <= 0:
+// the default 200 ms) and whether CTA 0 leaves its first k-block unissued, for
+// every later launch on that device.
+extern "C" int mm_debug_tc_fault(int device, int64_t wait_ns, int drop_first_load) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != device) MM_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  const unsigned long long ns = wait_ns > 0 ? (unsigned long long)wait_ns : (unsigned long long)TC_WAIT_NS;
+  const int drop = drop_first_load ? 1 : 0;
+  cudaError_t e = cudaMemcpyToSymbol(g_tc_wait_ns, &ns, sizeof(ns));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_tc_drop_first_load, &drop, sizeof(drop));
+  if (prev != device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "mm_debug_tc_fault");
   return MM_OK;
 }
 

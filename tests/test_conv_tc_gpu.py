@@ -187,3 +187,50 @@ def test_no_kernel_error_recorded(mm):
     code = ctypes.c_int(-1)
     _lib.check(_lib.load().mm_kernel_error(0, ctypes.byref(code), 0))
     assert code.value == 0
+
+
+@pytest.mark.parametrize("gather", [False, True])
+def test_tc_bounded_wait_runs_out_and_recovers(mm, gather):
+    """A device-side wait that runs out: with the test hook, CTA 0 leaves its
+    first k-block unissued and the wait budget is 1 ms, so a wait for that
+    stage gives up.  The kernel records an error code, finishes its own
+    in-flight copies and MMAs, frees its tensor memory and returns (the stream
+    synchronises; nothing hangs); the next launch with the defaults gives
+    correct results.  gather=True uses a 3 x 3 output, which no 128-pixel
+    rectangle covers well, so the producers gather A with cp.async;
+    gather=False a 32 x 40 output fetched by TMA rectangles."""
+    import ctypes
+    import time
+    from matrixman_b200 import runtime
+    lib = _lib.load()
+    dev = runtime.current_device()
+    rt = runtime.get_runtime(dev)
+    g = gen(91)
+    conv = nn.Conv2d(64, 64, 3, 1, 1, bias=True)
+    with torch.no_grad():
+        conv.weight.copy_(torch.randn(conv.weight.shape, generator=g) / 24.0)
+    unit = PreparedConv2d(conv, 2)
+    x = torch.rand(4, 64, 3, 3, generator=g) * 2 - 1 if gather else \
+        torch.rand(4, 64, 32, 40, generator=g) * 2 - 1
+    ref = ACTS[2](O.conv2d(x, conv.weight.detach(), conv.bias.detach(), 1, 1))
+    xd = nhwc(mm, x)
+    code = ctypes.c_int(-1)
+    with torch.no_grad():
+        assert max_rel_err(unit(xd).cpu(), ref) < CONV_GEMM_REL
+        _lib.check(lib.mm_kernel_error(dev, ctypes.byref(code), 1))
+        assert code.value == 0
+        _lib.check(lib.mm_debug_tc_fault(dev, 1_000_000, 1))
+        try:
+            t0 = time.perf_counter()
+            unit(xd)
+            rt.synchronize(timeout_ms=30_000)
+            elapsed = time.perf_counter() - t0
+            _lib.check(lib.mm_kernel_error(dev, ctypes.byref(code), 1))
+        finally:
+            _lib.check(lib.mm_debug_tc_fault(dev, 0, 0))
+        assert code.value in (1, 2, 3, 4), f"expected a wait error code, got {code.value}"
+        assert elapsed < 5.0
+        y = unit(xd).cpu()
+        _lib.check(lib.mm_kernel_error(dev, ctypes.byref(code), 0))
+    assert code.value == 0
+    assert max_rel_err(y, ref) < CONV_GEMM_REL
