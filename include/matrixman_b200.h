@@ -439,8 +439,9 @@ int mm_yolo_decode(const mm_tensor_t* const* feats, const float* strides, int nl
  * the reference accepts B = 1 only. */
 int mm_detect_reduce(const mm_tensor_t* pred, const mm_tensor_t* out, void* stream);
 
-/* Largest number of candidates (anchors at or above the confidence threshold)
- * one image may have in mm_detect_nms. */
+/* Candidates (anchors at or above the confidence threshold) per image that
+ * mm_detect_nms sorts and suppresses in shared memory; an image with more takes
+ * a slower global-memory pass with the same result. */
 #define MM_DETECT_MAX_CANDIDATES 12288
 
 /* Confidence filter, box conversion and per-class greedy NMS on the device, per
@@ -451,8 +452,9 @@ int mm_detect_reduce(const mm_tensor_t* pred, const mm_tensor_t* out, void* stre
  * earlier kept candidate of its class, in descending score order (equal scores
  * by anchor index).  dets [B, max_det, 6] receives the first max_det kept
  * (x1, y1, x2, y2, score, class) in descending score order and counts (device
- * int32[B]) their number; an image with more than MM_DETECT_MAX_CANDIDATES
- * candidates is skipped with counts[b] = -(candidates).  workspace: device
+ * int32[B]) their number.  The number of candidates per image is not limited
+ * (beyond MM_DETECT_MAX_CANDIDATES an image runs a global-memory pass; the
+ * reference's detections() has no cap either).  workspace: device
  * memory, 256-byte aligned, of at least mm_detect_nms_workspace_size bytes for
  * this batch and anchor count (it holds the candidates between the two
  * kernels); calls that run at the same time need separate workspaces. */

@@ -10,19 +10,25 @@
 //     classes, as torch's max/argmax) is >= conf_thr become candidates with
 //     corner boxes (cx - w/2, cy - h/2, cx + w/2, cy + h/2) clamped to
 //     [0, width-1] x [0, height-1]; candidates are ordered by score
-//     (descending; equal scores by anchor index), and greedy NMS keeps a
-//     candidate unless an earlier kept candidate of the same class overlaps it
+//     (descending; equal scores by class, then anchor index), and greedy NMS
+//     keeps a candidate unless an earlier kept candidate of the same class
+//     overlaps it
 //     with IoU > iou_thr (a candidate is kept only when IoU <= iou_thr, so a NaN
 //     IoU suppresses) -- the reference's per-class loop
 //     (demo/yolo_helpers.py:59-89, 91-137) restated as one pass over all
 //     classes, with its fp32 arithmetic in the same order (no contraction).
-//     The first max_det kept detections (x1, y1, x2, y2, score, class), in
-//     descending score order, go to dets[b]; counts[b] = their number.
+//     Within a class this order is the reference's (score, then input order);
+//     across classes it is the order of the reference's final sort of the kept
+//     detections by score (yolo_helpers.py:128), stable over its class-by-class
+//     list, so the kept list is already in output order.  The first max_det
+//     kept detections (x1, y1, x2, y2, score, class) go to dets[b];
+//     counts[b] = their number.
 //
-// One CTA per image holds its candidates' scores, classes and anchors in
-// shared memory (at most MM_DETECT_MAX_CANDIDATES); their boxes are recomputed
-// from the prediction (L2-resident) where needed.  An image with more
-// candidates is not processed and reports counts[b] = -(number of candidates).
+// One CTA per image sorts its candidates' keys and holds their boxes and
+// classes in shared memory (at most MM_DETECT_MAX_CANDIDATES of them).  An
+// image with more candidates runs a second, slower pass over the whole image
+// in global memory (detect_nms_large_kernel) with the same result, so the
+// number of candidates is not limited.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -47,6 +53,8 @@ struct DetArgs {
   int classes;
   float conf_thr, iou_thr, xmax, ymax;  // xmax = width - 1, ymax = height - 1
   int max_det;
+  int abits;  // anchor bits of a sort key (32 - class bits); 0: keys do not fit, every
+              // image with candidates takes the global-memory pass
   float* dets;
   int64_t ds0, ds1, ds2;  // strides of [B, max_det, 6]
   int32_t* counts;
@@ -134,14 +142,22 @@ __device__ __forceinline__ float4 det_box(const DetArgs& a, const float* pb, int
                      clampf_keep_nan(__fadd_rn(cx, hw), a.xmax), clampf_keep_nan(__fadd_rn(cy, hh), a.ymax));
 }
 
-// Sort key of a candidate: ascending keys = descending score, then ascending
-// anchor index.  The score's bits are mapped to an unsigned integer that
-// orders as the floats do (after -0 becomes +0, so equal scores give equal
-// high halves); NaN scores never reach here (they fail the filter).
-__device__ __forceinline__ unsigned long long det_key(float score, int anchor) {
+// High half of a sort key: ascending = descending score.  The score's bits
+// are mapped to an unsigned integer that orders as the floats do (after -0
+// becomes +0, so equal scores give equal halves); NaN scores never reach here
+// (they fail the filter).
+__device__ __forceinline__ unsigned det_score_key(float score) {
   unsigned u = __float_as_uint(__fadd_rn(score, 0.f));
   u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)(~u) << 32) | (unsigned)anchor;
+  return ~u;
+}
+
+// Sort key of a candidate: ascending keys = descending score, then ascending
+// class, then ascending anchor index (the low half holds the class above the
+// anchor's abits bits; the host picks abits so that both fit).
+__device__ __forceinline__ unsigned long long det_key(float score, int cls, int anchor, int abits) {
+  return ((unsigned long long)det_score_key(score) << 32) | ((unsigned long long)(unsigned)cls << abits) |
+         (unsigned)anchor;
 }
 
 // 1. Candidates, grid-wide: per anchor the best class (first maximum), the
@@ -180,7 +196,7 @@ __global__ void detect_candidates_kernel(DetArgs a, DetWork w) {
         const int64_t i = b * a.anchors + an;
         w.box[i] = det_box(a, pb, (int)an);
         w.sc[i] = make_float2(best, __int_as_float(bc));
-        if (slot < DET_CAP) w.keys[b * DET_CAP + slot] = det_key(best, (int)an);
+        if (slot < DET_CAP && a.abits > 0) w.keys[b * DET_CAP + slot] = det_key(best, bc, (int)an, a.abits);
       }
     }
   }
@@ -201,8 +217,8 @@ __global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a, DetW
   const int64_t b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
   const int n = w.count[b];
-  if (n > DET_CAP) {
-    if (tid == 0) a.counts[b] = -n;
+  if (n > DET_CAP || (a.abits == 0 && n > 0)) {
+    if (tid == 0) a.counts[b] = -n;  // left to detect_nms_large_kernel
     return;
   }
 
@@ -233,7 +249,7 @@ __global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a, DetW
 #pragma unroll
   for (int k = 0; k < DET_PER_THREAD; ++k) {
     const int j = tid + k * DET_THREADS;
-    an[k] = j < n ? (unsigned)key[j] : 0u;
+    an[k] = j < n ? (unsigned)key[j] & (unsigned)((1ull << a.abits) - 1ull) : 0u;
   }
   __syncthreads();
   const float4* wb = w.box + b * a.anchors;
@@ -308,6 +324,134 @@ __global__ void __launch_bounds__(DET_THREADS) detect_nms_kernel(DetArgs a, DetW
   if (tid == 0) a.counts[b] = nk;
 }
 
+// 5. Images with more candidates than the shared-memory pass holds
+// (detect_nms_kernel left counts[b] = -n): greedy NMS over the whole image in
+// global memory, one CTA per image (the others return at once).  The CTA marks
+// the image's candidates again (class -1 for the other anchors, whose
+// workspace entries the candidate pass did not write), then each round finds
+// the next candidate in NMS order -- the smallest (score key, class), then
+// the smallest anchor among the live ones with it: two block reductions --
+// keeps it and removes it and the later candidates of its class that overlap
+// it with IoU > iou_thr.  Same order, arithmetic and output as
+// detect_nms_kernel, without a limit on candidates, classes or anchors.
+
+// Minimum of v over the CTA (DET_THREADS threads), returned to every thread.
+__device__ __forceinline__ unsigned long long det_block_min(unsigned long long v, unsigned long long* red,
+                                                            unsigned long long* out) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, v, o);
+    v = other < v ? other : v;
+  }
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    v = lane < DET_THREADS / 32 ? red[lane] : ~0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, v, o);
+      v = other < v ? other : v;
+    }
+    if (lane == 0) *out = v;
+  }
+  __syncthreads();
+  return *out;
+}
+
+__global__ void __launch_bounds__(DET_THREADS) detect_nms_large_kernel(DetArgs a, DetWork w) {
+  const int64_t b = blockIdx.x;
+  if (a.counts[b] >= 0) return;
+  const int tid = threadIdx.x;
+  const float* pb = a.pred + b * a.ps0;
+  float2* sc = w.sc + b * a.anchors;
+  float4* bx = w.box + b * a.anchors;
+  for (int64_t an = tid; an < a.anchors; an += DET_THREADS) {
+    const float* p = pb + an * a.ps2;
+    float best = p[4 * a.ps1];
+    int bc = 0;
+    for (int c = 1; c < a.classes; ++c) {
+      const float v = p[(4 + c) * a.ps1];
+      if (v > best) {
+        best = v;
+        bc = c;
+      }
+    }
+    if (best >= a.conf_thr) {
+      bx[an] = det_box(a, pb, (int)an);
+      sc[an] = make_float2(best, __int_as_float(bc));
+    } else {
+      sc[an] = make_float2(0.f, __int_as_float(-1));
+    }
+  }
+  __syncthreads();
+  __shared__ unsigned long long red[DET_THREADS / 32];
+  __shared__ unsigned long long s_min;
+  float* db = a.dets + b * a.ds0;
+  int nk = 0;
+  while (nk < a.max_det) {
+    unsigned long long mk = ~0ull;
+    for (int64_t an = tid; an < a.anchors; an += DET_THREADS) {
+      const float2 v = sc[an];
+      const int c = __float_as_int(v.y);
+      if (c >= 0) {
+        const unsigned long long k = ((unsigned long long)det_score_key(v.x) << 32) | (unsigned)c;
+        mk = k < mk ? k : mk;
+      }
+    }
+    const unsigned long long key = det_block_min(mk, red, &s_min);
+    if (key == ~0ull) break;
+    // The smallest anchor with this score and class (its reduction may start
+    // only after every thread has read s_min: the first barrier inside).
+    unsigned long long ma = ~0ull;
+    for (int64_t an = tid; an < a.anchors; an += DET_THREADS) {
+      const float2 v = sc[an];
+      const int c = __float_as_int(v.y);
+      if (c >= 0 && (((unsigned long long)det_score_key(v.x) << 32) | (unsigned)c) == key) {
+        ma = (unsigned long long)an < ma ? (unsigned long long)an : ma;
+      }
+    }
+    const int i = (int)det_block_min(ma, red, &s_min);
+    const float4 cb = bx[i];
+    const float2 cv = sc[i];
+    const int ccls = __float_as_int(cv.y);
+    if (tid == 0) {
+      float* o = db + (int64_t)nk * a.ds1;
+      o[0] = cb.x;
+      o[a.ds2] = cb.y;
+      o[2 * a.ds2] = cb.z;
+      o[3 * a.ds2] = cb.w;
+      o[4 * a.ds2] = cv.x;
+      o[5 * a.ds2] = (float)ccls;
+    }
+    ++nk;
+    __syncthreads();  // every thread has read the kept candidate's entries
+    const float carea = __fmul_rn(__fsub_rn(cb.z, cb.x), __fsub_rn(cb.w, cb.y));
+    for (int64_t an = tid; an < a.anchors; an += DET_THREADS) {
+      const float2 v = sc[an];
+      if (__float_as_int(v.y) != ccls) continue;
+      if (an == i) {
+        sc[an].y = __int_as_float(-1);
+        continue;
+      }
+      const float4 rb = bx[an];
+      const float xx1 = tmax(rb.x, cb.x), yy1 = tmax(rb.y, cb.y);
+      const float xx2 = tmin(rb.z, cb.z), yy2 = tmin(rb.w, cb.w);
+      float iw = __fsub_rn(xx2, xx1), ih = __fsub_rn(yy2, yy1);
+      iw = iw < 0.f ? 0.f : iw;
+      ih = ih < 0.f ? 0.f : ih;
+      const float inter = __fmul_rn(iw, ih);
+      const float rarea = __fmul_rn(__fsub_rn(rb.z, rb.x), __fsub_rn(rb.w, rb.y));
+      float den = __fsub_rn(__fadd_rn(carea, rarea), inter);
+      den = den < 1e-12f ? 1e-12f : den;
+      const float iou = __fdiv_rn(inter, den);
+      if (!(iou <= a.iou_thr)) sc[an].y = __int_as_float(-1);
+    }
+    __syncthreads();
+  }
+  if (tid == 0) a.counts[b] = nk;
+}
+
 }  // namespace mm
 
 using namespace mm;
@@ -374,6 +518,11 @@ extern "C" int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_
   a.xmax = width - 1.0f;
   a.ymax = height - 1.0f;
   a.max_det = max_det;
+  {
+    int cbits = 0;  // bits of the largest class index
+    while ((1ll << cbits) < (long long)a.classes) ++cbits;
+    a.abits = a.anchors <= (1ll << (32 - cbits)) ? 32 - cbits : 0;
+  }
   a.dets = (float*)dets->data;
   a.ds0 = dets->stride[0]; a.ds1 = dets->stride[1]; a.ds2 = dets->stride[2];
   a.counts = counts;
@@ -406,6 +555,8 @@ extern "C" int mm_detect_nms(const mm_tensor_t* pred, float conf_thr, float iou_
   MM_LAUNCH_CHECK("mm_detect_nms candidate launch");
   detect_nms_kernel<<<(unsigned)a.batch, DET_THREADS, DET_SMEM, s>>>(a, w);
   MM_LAUNCH_CHECK("mm_detect_nms launch");
+  detect_nms_large_kernel<<<(unsigned)a.batch, DET_THREADS, 0, s>>>(a, w);
+  MM_LAUNCH_CHECK("mm_detect_nms large-image launch");
   return MM_OK;
 }
 

@@ -22,7 +22,10 @@ import torch
 from . import _lib, audit, ops, runtime
 from .tensor import MatrixManTensor
 
-MAX_CANDIDATES = 12288  # MM_DETECT_MAX_CANDIDATES in include/matrixman_b200.h
+# Candidates per image the shared-memory NMS pass holds
+# (MM_DETECT_MAX_CANDIDATES in include/matrixman_b200.h); images with more take
+# a global-memory pass, so this is a speed boundary, not a limit.
+MAX_CANDIDATES = 12288
 
 
 def _check_prediction(pred) -> tuple[int, int, int]:
@@ -54,8 +57,8 @@ def postprocess_detections(pred: MatrixManTensor, width: int, height: int,
     computed on the device.  Candidates are anchors whose best class score is
     >= ``conf_threshold``; boxes are clamped to [0, width-1] x [0, height-1];
     NMS is per class with IoU > ``iou_threshold`` suppressing.  At most
-    ``max_det`` detections per image are returned, and an image may have at
-    most 12288 candidates (raise ``conf_threshold`` otherwise)."""
+    ``max_det`` detections per image are returned; the number of candidates
+    is not limited."""
     b, _, _ = _check_prediction(pred)
     if max_det <= 0:
         raise ValueError("MatrixMan: max_det must be positive")
@@ -83,9 +86,8 @@ def postprocess_detections(pred: MatrixManTensor, width: int, height: int,
     result = []
     for i in range(b):
         n = host_counts[i]
-        if n < 0:
-            raise RuntimeError(f"MatrixMan: image {i} has {-n} candidates at confidence >= "
-                               f"{conf_threshold}; at most {MAX_CANDIDATES} are supported")
+        if n < 0 or n > max_det:
+            raise RuntimeError(f"MatrixMan: detection count {n} of image {i} is out of range")
         result.append([(row[:4], row[4], int(row[5]), names.get(int(row[5]), str(int(row[5]))))
                        for row in host[i, :n].tolist()])
     return result

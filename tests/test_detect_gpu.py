@@ -56,11 +56,27 @@ def test_nms_strided_view_and_max_det(mm):
     assert bit_exact(as_tensor(got[0]), want[:10])
 
 
-def test_nms_rejects_too_many_candidates(mm):
-    p = torch.rand(1, 6, 13000, generator=gen(2)) * 100
-    p[:, 4:] = 0.9
-    with pytest.raises(RuntimeError, match="candidates"):
-        mm.postprocess_detections(mm.to_device(p), 640, 640, 0.25, 0.45)
+@pytest.mark.parametrize("max_det", [300, 20000])
+def test_nms_beyond_shared_memory_capacity(mm, max_det):
+    """Images with more candidates than the shared-memory NMS pass holds
+    (12288) take the global-memory pass: same detections as the oracle, in the
+    same order, bit for bit.  Image 0 has 20000 candidates over 3 classes with
+    overlapping boxes and repeated scores; image 1 (about 7000 candidates,
+    repeated scores too) stays on the shared-memory pass in the same call.
+    Equal scores come out by class, then anchor, in both passes."""
+    g = gen(2)
+    a = 20000
+    p = torch.empty(2, 7, a)
+    p[:, 0:2] = torch.rand(2, 2, a, generator=g) * 1300 - 10
+    p[:, 2:4] = torch.rand(2, 2, a, generator=g) * 120 + 4
+    p[:, 4:] = torch.rand(2, 3, a, generator=g)
+    p[0, 4:] = (p[0, 4:] * 64).floor() / 64 * 0.7 + 0.3  # every anchor a candidate, ties
+    p[1, 4:] = (p[1, 4:] * 64).floor() / 64 * 0.35
+    got = mm.postprocess_detections(mm.to_device(p), 1280, 1280, 0.3, 0.45, max_det=max_det)
+    for i in range(2):
+        want = O.detections(p[i], 1280, 1280, 0.3, 0.45)[:max_det]
+        assert len(got[i]) == len(want)
+        assert bit_exact(as_tensor(got[i]), want)
 
 
 @pytest.mark.parametrize("batch,size", [(3, 256), (1, 640)])
