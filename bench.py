@@ -99,7 +99,8 @@ def parse_args():
                    help="run --steps eager forwards (no graphs, no timing) for an ncu capture")
     p.add_argument("--profile-conv", default=None, metavar="C,K,KSIZE,STRIDE,HW",
                    help="run one prepared convolution (SiLU epilogue) on a --batch x C x HW x HW "
-                        "NHWC input --steps + 1 times, for an ncu capture of one kernel")
+                        "input (NCHW for C <= 3, NHWC otherwise) --steps + 1 times, for an ncu "
+                        "capture of one kernel")
     return p.parse_args()
 
 
@@ -537,8 +538,11 @@ def run_profile_conv(args):
     g = torch.Generator().manual_seed(7)
     conv = nn.Conv2d(c, k, ks, st, ks // 2)
     unit = PreparedConv2d(conv, 2)
-    x = torch.rand(args.batch, hw, hw, c, generator=g) * 2 - 1
-    xd = matrixman.to_device(x).permute(0, 3, 1, 2)
+    if c <= 3:  # stems read the image planes (NCHW), as in a model's first layer
+        xd = matrixman.to_device(torch.rand(args.batch, c, hw, hw, generator=g) * 2 - 1)
+    else:
+        x = torch.rand(args.batch, hw, hw, c, generator=g) * 2 - 1
+        xd = matrixman.to_device(x).permute(0, 3, 1, 2)
     with torch.no_grad():
         for _ in range(args.steps + 1):
             y = unit(xd)

@@ -89,6 +89,36 @@ def test_conv_shapes_nchw_and_nhwc(mm, c, k, ksz, stride, pad, dil, groups, hw, 
     assert max_rel_err(y2, ref) < CONV_GEMM_REL
 
 
+@pytest.mark.parametrize("c,k,h,w,n", [
+    (3, 16, 64, 65, 2),    # odd input width: a partial last quad of output columns
+    (3, 48, 31, 33, 1),    # three 16-channel groups, odd sizes
+    (1, 16, 67, 67, 1),
+    (2, 32, 9, 12, 3),     # tiny images: every quad touches an edge
+    (3, 16, 640, 640, 1),  # the YOLOv8 stem
+])
+def test_stride2_stem_kernel(mm, c, k, h, w, n):
+    """Stride-2 3x3 stems with channels-last output run the 4-pixel stem
+    kernel (prepared convolution); NCHW output runs the one-pixel kernel
+    (eager F.conv2d).  Both accumulate each output in the same order, so
+    they agree bit for bit; both are within the convolution tolerance of the
+    oracle, with and without the fused SiLU."""
+    from matrixman_b200.preparation import PreparedConv2d
+    g = gen(c * 1000 + k + h)
+    x = torch.rand(n, c, h, w, generator=g) * 2 - 1
+    conv = torch.nn.Conv2d(c, k, 3, 2, 1)
+    with torch.no_grad():
+        conv.weight.copy_(torch.randn(k, c, 3, 3, generator=g) * (1.0 / (c * 9) ** 0.5))
+        conv.bias.copy_(torch.randn(k, generator=g) * 0.1)
+        xd = mm.to_device(x)
+        y_stem = PreparedConv2d(conv, 0)(xd).cpu()
+        y_silu = PreparedConv2d(conv, 2)(xd).cpu()
+        y_pixel = F.conv2d(dev(mm, x), conv.weight, conv.bias, 2, 1).cpu()
+    ref = O.conv2d(x, conv.weight.detach(), conv.bias.detach(), 2, 1)
+    assert bit_exact(y_stem, y_pixel)
+    assert max_rel_err(y_stem, ref) < CONV_GEMM_REL
+    assert max_rel_err(y_silu, ref * torch.sigmoid(ref)) < CONV_GEMM_REL
+
+
 def test_conv_empty_and_unsupported(mm):
     x = dev(mm, torch.randn(1, 4, 8, 8))
     with pytest.raises(NotImplementedError):
