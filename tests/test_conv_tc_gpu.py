@@ -82,6 +82,34 @@ def test_tc_precision_is_fp32_class(mm):
     assert err < 1e-5
 
 
+@pytest.mark.parametrize("act", [2, 3])
+def test_tc_fused_activation_accuracy(mm, act):
+    """The fused SiLU / sigmoid element by element: the same 1x1 convolution
+    (identity weights, inputs spread over [-100, 100]) with and without the
+    activation; every activated element is within 1e-5 relative of the
+    double-precision activation of the un-activated output (absolute 1e-30
+    where it underflows).  The bar covers the fast exponential's documented
+    error, 2 + 1.173 |x| ulp (about 6e-6 relative at |x| = 88), and the fast
+    division's 2 ulp."""
+    c = 32
+    conv = nn.Conv2d(c, c, 1, 1, 0, bias=True)
+    with torch.no_grad():
+        conv.weight.copy_(torch.eye(c).reshape(c, c, 1, 1))
+        conv.bias.zero_()
+    x = torch.linspace(-100.0, 100.0, 4 * 64 * 64 * c).reshape(4, c, 64, 64)
+    x[0, 0, 0, :8] = torch.tensor([0.0, -0.0, 1e-30, -1e-30, 80.5, -80.5, 87.0, -87.0])
+    xd = nhwc(mm, x)
+    with torch.no_grad():
+        pre = PreparedConv2d(conv, 0)(xd).cpu().double()
+        y = PreparedConv2d(conv, act)(xd).cpu().double()
+    ref = pre * torch.sigmoid(pre) if act == 2 else torch.sigmoid(pre)
+    err = (y - ref).abs()
+    bad = err > 1e-5 * ref.abs() + 1e-30
+    i = int(torch.argmax((err / (ref.abs() + 1e-30)).flatten()))
+    assert not bool(bad.any()), (int(bad.sum()), float(pre.flatten()[i]), float(y.flatten()[i]),
+                                 float(ref.flatten()[i]))
+
+
 def test_tc_channel_slices_in_and_out(mm):
     from matrixman_b200 import ops
     from matrixman_b200.preparation import _channel_slice
