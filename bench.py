@@ -397,23 +397,29 @@ def run_b200(args, spec):
 
 
 CONV_ENTRIES = ("mm_conv2d", "mm_conv2d_tc", "mm_gemm")
-TRAFFIC_SUMMARY = ROOT / "profiles" / "conv_tc_yolov8n_bs64_traffic.md"
+TRAFFIC_SUMMARY = ROOT / "profiles" / "conv_tc_c64_80x80_bs128.md"
 
 
 def conv_traffic_per_launch():
-    """DRAM bytes (read + write) per conv launch from the committed ncu summary
-    of one bs64 forward (line ``bytes_per_launch: N``), or None."""
+    """DRAM bytes (read + write) of one launch of the tensor-core convolution
+    from the committed one-launch ncu capture of a representative YOLOv8n
+    layer (lines ``bytes_per_launch:``, ``algorithmic_bytes_per_launch:`` and
+    ``layer:``), or None."""
     if not TRAFFIC_SUMMARY.exists():
         return None
+    fields = {}
     for line in TRAFFIC_SUMMARY.read_text().splitlines():
-        if line.strip().startswith("bytes_per_launch:"):
-            try:
-                return {"bytes_per_launch": int(float(line.split(":", 1)[1].strip())),
-                        "source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, "
-                                  f"{TRAFFIC_SUMMARY.relative_to(ROOT)}"}
-            except ValueError:
-                return None
-    return None
+        key, sep, val = line.partition(":")
+        if sep and key.strip() in ("bytes_per_launch", "algorithmic_bytes_per_launch", "layer"):
+            fields[key.strip()] = val.strip()
+    try:
+        return {"bytes_per_launch": int(float(fields["bytes_per_launch"])),
+                "algorithmic_bytes_per_launch": int(float(fields["algorithmic_bytes_per_launch"])),
+                "layer": fields.get("layer", ""),
+                "source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
+                          f"{TRAFFIC_SUMMARY.relative_to(ROOT)}"}
+    except (KeyError, ValueError):
+        return None
 
 
 def roofline(res: dict, spec=None) -> tuple[dict, int, dict]:
@@ -438,7 +444,8 @@ def roofline(res: dict, spec=None) -> tuple[dict, int, dict]:
     peak = peaks["bf16_tflops_sustained"]
     ceiling = peak / 6.0
     kernels_per_forward = sum(v["launches"] for v in summary.values())
-    # (the committed DRAM-traffic capture covers the YOLOv8n batch-64 forward)
+    # (the committed DRAM-traffic capture is one launch of a YOLOv8n layer; the
+    # kernel moves its algorithmic bytes about once, so traffic ~ algorithmic)
     traffic = conv_traffic_per_launch() if spec is None or spec.key == "y8n" else None
     roof = {"bound": "tensor", "kernel": "+".join(k for k in CONV_ENTRIES if k in summary),
             "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
@@ -452,6 +459,8 @@ def roofline(res: dict, spec=None) -> tuple[dict, int, dict]:
             "forward_ms_eager_events": round(total_ms, 3)}
     if traffic:
         roof["traffic_source"] = traffic["source"]
+        roof["traffic_layer"] = traffic["layer"]
+        roof["traffic_algorithmic_bytes"] = traffic["algorithmic_bytes_per_launch"]
     shares = {k: {"launches": v["launches"], "ms": round(v["ms"], 4), "share": round(v["ms"] / total_ms, 4)}
               for k, v in sorted(summary.items(), key=lambda kv: -kv[1]["ms"])}
     return roof, kernels_per_forward, shares
