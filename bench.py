@@ -396,7 +396,7 @@ def run_b200(args, spec):
             "matrixman": matrixman, "dist": dist if world > 1 else None}
 
 
-CONV_ENTRIES = ("mm_conv2d", "mm_conv2d_tc", "mm_gemm")
+CONV_ENTRIES = ("mm_conv2d", "mm_conv2d_region", "mm_conv2d_tc", "mm_conv2d_tc_region", "mm_gemm")
 TRAFFIC_SUMMARY = ROOT / "profiles" / "conv_tc_c64_80x80_bs128.md"
 
 

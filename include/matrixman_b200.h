@@ -385,6 +385,20 @@ int mm_conv2d(const mm_tensor_t* x, const mm_tensor_t* w, const float* bias,
               const mm_tensor_t* residual, const mm_conv_params_t* p, const mm_tensor_t* y,
               void* stream);
 
+/* One region of a convolution's output: output rows [row0, row0 + H) and
+ * columns [col0, col0 + W), where H x W is y's spatial size (y, and the
+ * residual if given, are views of that region; p describes the whole
+ * convolution).  The region reads the input rows and columns the whole
+ * convolution would read for it (padding applies only at the image borders)
+ * and each output value is computed in the same order, so tiling an output
+ * into regions gives the same result bit for bit.  The CUDA mapping of the
+ * reference's tileLimit (config.py:305-314; consumed by the OpenGL convolution,
+ * backends/opengl/convolution.py:1299), which bounds the extent of one
+ * convolution pass. */
+int mm_conv2d_region(const mm_tensor_t* x, const mm_tensor_t* w, const float* bias,
+                     const mm_tensor_t* residual, const mm_conv_params_t* p, int64_t row0, int64_t col0,
+                     const mm_tensor_t* y, void* stream);
+
 /* 3xTF32 tensor-core convolution on a prepacked weight: w_hi/w_lo are
  * [K_pad][R*S][C_pad] (C_pad % 32 == 0, K_pad % 16 == 0) with the tf32 high part
  * and the fp32 remainder of each weight.  x/y/residual must be NHWC views
@@ -394,6 +408,14 @@ int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float* w_lo, int
                  int r, int s, int c_pad, int k_pad, const float* bias,
                  const mm_tensor_t* residual, const mm_conv_params_t* p, const mm_tensor_t* y,
                  void* stream);
+
+/* mm_conv2d_tc for one region of the output (rows [row0, row0 + H), columns
+ * [col0, col0 + W) of y's H x W), with the same bit-for-bit guarantee as
+ * mm_conv2d_region; the tensor-core counterpart of the same tileLimit mapping. */
+int mm_conv2d_tc_region(const mm_tensor_t* x, const float* w_hi, const float* w_lo, int k_out, int c_in,
+                        int r, int s, int c_pad, int k_pad, const float* bias,
+                        const mm_tensor_t* residual, const mm_conv_params_t* p, int64_t row0,
+                        int64_t col0, const mm_tensor_t* y, void* stream);
 
 /* Error code recorded by a device-side bounded wait that gave up (0 = none);
  * clear != 0 resets it.  Kernels never trap: a stuck pipeline records the code,

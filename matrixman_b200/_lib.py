@@ -174,6 +174,9 @@ SIGNATURES = {
     "mm_conv2d": [_T, _T, _fp, _T, ctypes.POINTER(MMConvParams), _T, _vp],
     "mm_conv2d_tc": [_T, _fp, _fp, _i, _i, _i, _i, _i, _i, _fp, _T,
                      ctypes.POINTER(MMConvParams), _T, _vp],
+    "mm_conv2d_region": [_T, _T, _fp, _T, ctypes.POINTER(MMConvParams), _i64, _i64, _T, _vp],
+    "mm_conv2d_tc_region": [_T, _fp, _fp, _i, _i, _i, _i, _i, _i, _fp, _T,
+                            ctypes.POINTER(MMConvParams), _i64, _i64, _T, _vp],
     "mm_tf32_split": [_fp, _fp, _fp, _i64, _vp],
     "mm_ipc_alloc": [_i, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _vp],
     "mm_ipc_free": [_i, _vp],

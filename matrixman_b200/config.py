@@ -22,12 +22,14 @@ B200 meaning of the north-star knobs:
   reusable immediately (ordering as above); ``deferred``: released blocks stay
   pending until their release event has completed.
 * ``tile_limit`` -- validated, stored and reported with the reference's rules
-  (a positive integer or ``auto``), and locked after init like the other
-  runtime fields.  It has no effect on CUDA: the reference uses it to bound
-  the physical OpenGL texture tile a convolution renders into
-  (backends/opengl/convolution.py:1299-1320), a graphics-API size limit that
-  device buffers on B200 do not have, so every convolution runs as one
-  launch over its whole output.
+  (a positive integer or ``auto``; default 256), and locked after init like
+  the other runtime fields.  The reference uses it to bound the physical
+  OpenGL tile a convolution renders into (backends/opengl/convolution.py:1299).
+  On CUDA an integer limit bounds the extent of one convolution launch: an
+  output wider or taller than the limit runs as several launches of at most
+  limit x limit output pixels each (mm_conv2d_region / mm_conv2d_tc_region),
+  with the same result bit for bit; ``auto`` means one launch per
+  convolution, whatever its size.
 
 Settings without a CUDA meaning (OpenGL diagnostics) are accepted and
 reported so that existing scripts keep working; they have no effect.
@@ -55,7 +57,7 @@ _FIELDS: dict[str, tuple] = {
     "useDGPU": (False, "MATRIXMAN_USE_DGPU", "use_dgpu", "Backend / device", "backend-specific",
                 "Requests a discrete adapter (no effect on CUDA)."),
     "tileLimit": (256, "MATRIXMAN_TILE_LIMIT", "tile_limit", "OpenGL tiling", "stable",
-                  "Maximum OpenGL tile dimension (accepted and reported; no effect on CUDA)."),
+                  "Largest output rows/columns of one convolution launch (auto: no limit)."),
     "tileSync": ("per_tile", "MATRIXMAN_TILE_SYNC", "tile_sync", "OpenGL tiling", "stable",
                  "Tiled-convolution synchronization (no effect on CUDA)."),
     "syncPolicy": ("safe", "MATRIXMAN_SYNC_POLICY", "sync_policy", "Synchronization", "stable",

@@ -322,10 +322,12 @@ __global__ void __launch_bounds__(128) conv_smallc_kernel(ConvArgs a, int vec_st
   }
 }
 
-// Stride-2 3x3 stems (pad 1, dilation 1) with channels-last output: each
-// thread computes PX neighbouring output pixels of a row x 16 output channels.
-// The PX pixels read input columns 2*PX*j - 1 .. 2*PX*j + 2*PX - 1 of each
-// (channel, row) -- PX/2 aligned float4 loads and one scalar -- and each
+// Stride-2 3x3 stems (dilation 1, any padding: negative padding is a region
+// of a larger convolution's output) with channels-last output: each thread
+// computes PX neighbouring output pixels of a row x 16 output channels.  The
+// PX pixels read input columns 2*PX*j - pw .. 2*PX*j - pw + 2*PX of each
+// (channel, row) -- with pw = 1 (odd padding in general, and regions starting
+// at an even column), PX/2 aligned float4 loads and one scalar -- and each
 // weight tap, one broadcast read of 4 float4 from shared memory, feeds 16*PX
 // FMAs (16 in the one-pixel kernel above, whose shared-memory reads were its
 // limit).  Same FMA order per output as conv_smallc_kernel (channel, row,
@@ -357,8 +359,9 @@ __global__ void __launch_bounds__(128) conv_stem_s2_kernel(ConvArgs a, int64_t q
     const int64_t t = q / qw;
     const int oh_ = (int)(t % a.oh);
     const int n_ = (int)(t / a.oh);
-    const int col0 = 2 * PX * j - 1;  // input column of tap s = 0 for the first pixel
-    const bool full = col0 >= 0 && col0 + NV - 1 < a.w_in;
+    const int col0 = 2 * PX * j - a.pw;  // input column of tap s = 0 for the first pixel
+    // (vector loads when the span is inside the row and col0 + 1 is 16-byte aligned)
+    const bool full = col0 >= 0 && col0 + NV - 1 < a.w_in && ((col0 + 1) & 3) == 0;
     const float* xb = a.x + (int64_t)n_ * a.xs[0];
     float acc[PX][SC_KT];
 #pragma unroll
@@ -369,7 +372,7 @@ __global__ void __launch_bounds__(128) conv_stem_s2_kernel(ConvArgs a, int64_t q
     for (int c = 0; c < CIN; ++c) {
 #pragma unroll
       for (int r = 0; r < 3; ++r) {
-        const int ih = 2 * oh_ - 1 + r;
+        const int ih = 2 * oh_ - a.ph + r;
         float v[NV];
         if ((unsigned)ih < (unsigned)a.h) {
           const float* row = xb + c * a.xs[1] + (int64_t)ih * a.xs[2];
@@ -426,11 +429,11 @@ __global__ void __launch_bounds__(128) conv_stem_s2_kernel(ConvArgs a, int64_t q
   }
 }
 
-// The stem kernel applies: stride 2, 3x3, pad 1, dilation 1, no residual,
+// The stem kernel applies: stride 2, 3x3, dilation 1 (any padding), no residual,
 // Kout a multiple of 16, unit-stride input rows and channels-last output whose
 // float4 accesses stay aligned.
 bool stem_s2_applies(const ConvArgs& a, int vec_store) {
-  return vec_store && a.r == 3 && a.s == 3 && a.sh == 2 && a.sw == 2 && a.ph == 1 && a.pw == 1 &&
+  return vec_store && a.r == 3 && a.s == 3 && a.sh == 2 && a.sw == 2 &&
          a.dh == 1 && a.dw == 1 && a.res == nullptr && a.kout % SC_KT == 0 && a.xs[3] == 1 &&
          a.xs[0] % 4 == 0 && a.xs[1] % 4 == 0 && a.xs[2] % 4 == 0 && (((uintptr_t)a.x) & 15) == 0;
 }
@@ -495,9 +498,17 @@ int conv_simt_dispatch(const ConvArgs& a, bool cfast, cudaStream_t s) {
 
 using namespace mm;
 
-extern "C" int mm_conv2d(const mm_tensor_t* x, const mm_tensor_t* w, const float* bias,
-                         const mm_tensor_t* residual, const mm_conv_params_t* p,
-                         const mm_tensor_t* y, void* stream) {
+namespace {
+
+// The convolution's output pixels [row0, row0 + H) x [col0, col0 + W) of
+// y's H x W (region == true), or its whole output.  A region is the same
+// convolution with effective padding pad - row0 * stride (negative inside the
+// image); every kernel here computes input coordinates as o * stride - pad +
+// tap with bounds checks, so a region reads what the full convolution would
+// and accumulates each output pixel in the same order.
+int conv2d_impl(const mm_tensor_t* x, const mm_tensor_t* w, const float* bias, const mm_tensor_t* residual,
+                const mm_conv_params_t* p, bool region, int64_t row0, int64_t col0, const mm_tensor_t* y,
+                void* stream) {
   int rc;
   if ((rc = validate(x, "mm_conv2d input", MM_F32)) != MM_OK) return rc;
   if ((rc = validate(w, "mm_conv2d weight", MM_F32)) != MM_OK) return rc;
@@ -545,11 +556,20 @@ extern "C" int mm_conv2d(const mm_tensor_t* x, const mm_tensor_t* w, const float
     return fail(MM_ERR_UNSUPPORTED, "mm_conv2d: invalid stride, padding, or dilation");
   a.cg = a.c / a.groups;
   a.kg = a.kout / a.groups;
-  int64_t oh = ((int64_t)a.h + 2 * a.ph - (int64_t)a.dh * (a.r - 1) - 1) / a.sh + 1;
-  int64_t ow = ((int64_t)a.w_in + 2 * a.pw - (int64_t)a.dw * (a.s - 1) - 1) / a.sw + 1;
-  if (oh <= 0 || ow <= 0) return fail(MM_ERR_INVALID, "mm_conv2d: output dimensions must be positive");
-  if (y->size[0] != a.n || y->size[1] != a.kout || y->size[2] != oh || y->size[3] != ow)
+  const int64_t oh_full = ((int64_t)a.h + 2 * a.ph - (int64_t)a.dh * (a.r - 1) - 1) / a.sh + 1;
+  const int64_t ow_full = ((int64_t)a.w_in + 2 * a.pw - (int64_t)a.dw * (a.s - 1) - 1) / a.sw + 1;
+  if (oh_full <= 0 || ow_full <= 0)
+    return fail(MM_ERR_INVALID, "mm_conv2d: output dimensions must be positive");
+  if (y->size[0] != a.n || y->size[1] != a.kout)
     return fail(MM_ERR_INVALID, "mm_conv2d: output shape mismatch");
+  if (!region && (y->size[2] != oh_full || y->size[3] != ow_full))
+    return fail(MM_ERR_INVALID, "mm_conv2d: output shape mismatch");
+  if (region && (row0 < 0 || col0 < 0 || y->size[2] <= 0 || y->size[3] <= 0 ||
+                 row0 + y->size[2] > oh_full || col0 + y->size[3] > ow_full))
+    return fail(MM_ERR_INVALID, "mm_conv2d_region: region outside the convolution's output");
+  const int64_t oh = y->size[2], ow = y->size[3];
+  a.ph = (int)(a.ph - row0 * a.sh);  // effective padding of the region (< 0 inside)
+  a.pw = (int)(a.pw - col0 * a.sw);
   if (residual) {
     for (int i = 0; i < 4; ++i)
       if (residual->size[i] != y->size[i]) return fail(MM_ERR_INVALID, "mm_conv2d: residual shape mismatch");
@@ -570,6 +590,20 @@ extern "C" int mm_conv2d(const mm_tensor_t* x, const mm_tensor_t* w, const float
   // Channel-fastest K order when channels are the densest input dim (NHWC).
   bool cfast = x->stride[1] == 1 && a.c > 1;
   return conv_simt_dispatch(a, cfast, resolve_stream(stream));
+}
+
+}  // namespace
+
+extern "C" int mm_conv2d(const mm_tensor_t* x, const mm_tensor_t* w, const float* bias,
+                         const mm_tensor_t* residual, const mm_conv_params_t* p,
+                         const mm_tensor_t* y, void* stream) {
+  return conv2d_impl(x, w, bias, residual, p, false, 0, 0, y, stream);
+}
+
+extern "C" int mm_conv2d_region(const mm_tensor_t* x, const mm_tensor_t* w, const float* bias,
+                                const mm_tensor_t* residual, const mm_conv_params_t* p, int64_t row0,
+                                int64_t col0, const mm_tensor_t* y, void* stream) {
+  return conv2d_impl(x, w, bias, residual, p, true, row0, col0, y, stream);
 }
 
 extern "C" int mm_gemm(const mm_tensor_t* x, const mm_tensor_t* w, const mm_tensor_t* bias,

@@ -1440,12 +1440,17 @@ bool nhwc_ok(const mm_tensor_t* t) {
          t->stride[3] % 4 == 0 && aligned16(t->data);
 }
 
-}  // namespace
-
-extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float* w_lo, int k_out,
-                            int c_in, int r, int s, int c_pad, int k_pad, const float* bias,
-                            const mm_tensor_t* residual, const mm_conv_params_t* p,
-                            const mm_tensor_t* y, void* stream) {
+// The convolution's output pixels [row0, row0 + H) x [col0, col0 + W) of
+// y's H x W (region == true), or its whole output (region == false, y must be
+// the full output).  A region is the same convolution with effective padding
+// pad - row0 * stride (negative inside the image): every A mode computes its
+// input coordinates as o * stride - pad + tap and reads taps outside the
+// image as zero, so a region reads exactly the rows and columns the full
+// convolution would, and each output pixel is accumulated in the same order.
+int conv2d_tc_impl(const mm_tensor_t* x, const float* w_hi, const float* w_lo, int k_out, int c_in, int r,
+                   int s, int c_pad, int k_pad, const float* bias, const mm_tensor_t* residual,
+                   const mm_conv_params_t* p, bool region, int64_t row0, int64_t col0, const mm_tensor_t* y,
+                   void* stream) {
   int rc;
   if ((rc = validate(x, "mm_conv2d_tc input", MM_F32)) != MM_OK) return rc;
   if ((rc = validate(y, "mm_conv2d_tc output", MM_F32)) != MM_OK) return rc;
@@ -1466,11 +1471,17 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
       p->pad_w < 0 || r <= 0 || s <= 0)
     return fail(MM_ERR_INVALID, "mm_conv2d_tc: invalid geometry");
   const int64_t n = x->size[0], h = x->size[2], w = x->size[3];
-  const int64_t oh = (h + 2 * p->pad_h - (int64_t)p->dil_h * (r - 1) - 1) / p->stride_h + 1;
-  const int64_t ow = (w + 2 * p->pad_w - (int64_t)p->dil_w * (s - 1) - 1) / p->stride_w + 1;
-  if (oh <= 0 || ow <= 0) return fail(MM_ERR_INVALID, "mm_conv2d_tc: empty output");
-  if (y->size[0] != n || y->size[1] != k_out || y->size[2] != oh || y->size[3] != ow)
+  const int64_t oh_full = (h + 2 * p->pad_h - (int64_t)p->dil_h * (r - 1) - 1) / p->stride_h + 1;
+  const int64_t ow_full = (w + 2 * p->pad_w - (int64_t)p->dil_w * (s - 1) - 1) / p->stride_w + 1;
+  if (oh_full <= 0 || ow_full <= 0) return fail(MM_ERR_INVALID, "mm_conv2d_tc: empty output");
+  if (y->size[0] != n || y->size[1] != k_out)
     return fail(MM_ERR_INVALID, "mm_conv2d_tc: output shape mismatch");
+  if (!region && (y->size[2] != oh_full || y->size[3] != ow_full))
+    return fail(MM_ERR_INVALID, "mm_conv2d_tc: output shape mismatch");
+  if (region && (row0 < 0 || col0 < 0 || y->size[2] <= 0 || y->size[3] <= 0 ||
+                 row0 + y->size[2] > oh_full || col0 + y->size[3] > ow_full))
+    return fail(MM_ERR_INVALID, "mm_conv2d_tc_region: region outside the convolution's output");
+  const int64_t oh = y->size[2], ow = y->size[3];
   if (residual) {
     for (int i = 0; i < 4; ++i)
       if (residual->size[i] != y->size[i]) return fail(MM_ERR_INVALID, "mm_conv2d_tc: residual shape");
@@ -1489,7 +1500,9 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
   a.bias = bias;
   a.h = (int)h; a.w = (int)w; a.c = c_in;
   a.oh = (int)oh; a.ow = (int)ow; a.kout = k_out;
-  a.r = r; a.s = s; a.sh = p->stride_h; a.sw = p->stride_w; a.ph = p->pad_h; a.pw = p->pad_w;
+  a.r = r; a.s = s; a.sh = p->stride_h; a.sw = p->stride_w;
+  a.ph = (int)(p->pad_h - row0 * p->stride_h);  // effective padding of the region (< 0 inside)
+  a.pw = (int)(p->pad_w - col0 * p->stride_w);
   a.dh = p->dil_h; a.dw = p->dil_w;
   if (m_total > 0x7fffffffLL - TC_BM) return fail(MM_ERR_UNSUPPORTED, "mm_conv2d_tc: too many output pixels");
   {
@@ -1550,7 +1563,7 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
     // TMA traversal strides go up to 8; the box spans tw * stride input columns.
     const bool strided_ok = p->stride_h <= 8 && p->stride_w <= 8;
     const bool uniform = x->stride[2] == w * x->stride[3] && x->stride[0] == h * x->stride[2];
-    if (stride1 && r == 1 && s == 1 && p->pad_h == 0 && p->pad_w == 0 && uniform &&
+    if (!region && stride1 && r == 1 && s == 1 && p->pad_h == 0 && p->pad_w == 0 && uniform &&
         n * h * w <= 0x7fffffffLL) {
       a.amode = TC_A_FLAT;
     } else if (strided_ok) {
@@ -1726,6 +1739,24 @@ extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float
           "mm_conv2d_tc launch");
   MM_LAUNCH_CHECK("mm_conv2d_tc launch");
   return MM_OK;
+}
+
+}  // namespace
+
+extern "C" int mm_conv2d_tc(const mm_tensor_t* x, const float* w_hi, const float* w_lo, int k_out,
+                            int c_in, int r, int s, int c_pad, int k_pad, const float* bias,
+                            const mm_tensor_t* residual, const mm_conv_params_t* p,
+                            const mm_tensor_t* y, void* stream) {
+  return conv2d_tc_impl(x, w_hi, w_lo, k_out, c_in, r, s, c_pad, k_pad, bias, residual, p, false, 0, 0, y,
+                        stream);
+}
+
+extern "C" int mm_conv2d_tc_region(const mm_tensor_t* x, const float* w_hi, const float* w_lo, int k_out,
+                                   int c_in, int r, int s, int c_pad, int k_pad, const float* bias,
+                                   const mm_tensor_t* residual, const mm_conv_params_t* p, int64_t row0,
+                                   int64_t col0, const mm_tensor_t* y, void* stream) {
+  return conv2d_tc_impl(x, w_hi, w_lo, k_out, c_in, r, s, c_pad, k_pad, bias, residual, p, true, row0, col0,
+                        y, stream);
 }
 
 // Test hook for the bounded-wait error path (no counterpart in the

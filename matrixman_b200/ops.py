@@ -349,8 +349,46 @@ def conv_output_hw(h, w, r, s, stride, padding, dilation):
     return oh, ow
 
 
+_FROM_CONFIG = object()
+
+
+def conv_tile_cap(cap=_FROM_CONFIG):
+    """Largest output extent (rows and columns) of one convolution launch.
+
+    The reference's ``tileLimit`` bounds the physical tile one convolution pass
+    renders into (drivers/matrixman/config.py:305-314, consumed at
+    backends/opengl/convolution.py:1299); on CUDA an integer limit caps each
+    launch at limit x limit output pixels, and ``auto`` means no cap (device
+    buffers have no texture-size limit).  ``cap`` overrides the setting
+    (None: no cap)."""
+    if cap is _FROM_CONFIG:
+        value = config.tileLimit
+        return None if value == "auto" else int(value)
+    return None if cap is None else int(cap)
+
+
+def conv_regions(oh: int, ow: int, cap) -> list[tuple[int, int, int, int]]:
+    """(row0, col0, rows, cols) regions covering an oh x ow output, row-major,
+    at most cap x cap pixels each; one region when cap is None or the output
+    fits."""
+    if cap is None or (oh <= cap and ow <= cap):
+        return [(0, 0, oh, ow)]
+    if cap <= 0:
+        raise ValueError("MatrixMan: tile limit must be positive")
+    return [(r0, c0, min(cap, oh - r0), min(cap, ow - c0))
+            for r0 in range(0, oh, cap) for c0 in range(0, ow, cap)]
+
+
+def _region_view(t: MatrixManTensor, r0: int, c0: int, rows: int, cols: int) -> MatrixManTensor:
+    """Rows [r0, r0 + rows) and columns [c0, c0 + cols) of an N, C, H, W view."""
+    st = t._logical_strides
+    shape = (int(t.shape[0]), int(t.shape[1]), rows, cols)
+    return MatrixManTensor._from_owner(t._owner, shape, t._storage_offset + r0 * st[2] + c0 * st[3], st)
+
+
 def convolution(x, weight, bias, stride, padding, dilation, groups, *, act=_lib.ACT_NONE,
-                residual=None, residual_before_act=False, out=None, out_strides=None) -> MatrixManTensor:
+                residual=None, residual_before_act=False, out=None, out_strides=None,
+                tile_cap=_FROM_CONFIG) -> MatrixManTensor:
     x = require_mm(x, "convolution")
     if x.dtype != F32 or x.dim() != 4:
         raise NotImplementedError("MatrixMan/CUDA: only float32 NCHW convolution is implemented")
@@ -389,44 +427,64 @@ def convolution(x, weight, bias, stride, padding, dilation, groups, *, act=_lib.
         out = empty(rt, shape, out_strides)
     params = _lib.MMConvParams(stride[0], stride[1], padding[0], padding[1], dilation[0], dilation[1],
                                groups, int(act), 1 if residual_before_act else 0, 0)
-    res_desc = residual.desc() if residual is not None else None
-    _launch("mm_conv2d", _p(x.desc()), _p(w.desc()),
-            ctypes.c_void_p(b.element_ptr) if b is not None else None,
-            _p(res_desc) if res_desc is not None else None,
-            ctypes.byref(params), _p(out.desc()), rt.stream)
+    bias_ptr = ctypes.c_void_p(b.element_ptr) if b is not None else None
+    regions = conv_regions(oh, ow, conv_tile_cap(tile_cap))
+    if len(regions) == 1:
+        res_desc = residual.desc() if residual is not None else None
+        _launch("mm_conv2d", _p(x.desc()), _p(w.desc()), bias_ptr,
+                _p(res_desc) if res_desc is not None else None,
+                ctypes.byref(params), _p(out.desc()), rt.stream)
+        return out
+    for r0, c0, rows, cols in regions:
+        y = _region_view(out, r0, c0, rows, cols)
+        res_desc = _region_view(residual, r0, c0, rows, cols).desc() if residual is not None else None
+        _launch("mm_conv2d_region", _p(x.desc()), _p(w.desc()), bias_ptr,
+                _p(res_desc) if res_desc is not None else None, ctypes.byref(params),
+                ctypes.c_int64(r0), ctypes.c_int64(c0), _p(y.desc()), rt.stream)
     return out
 
 
 def conv_tc(x: MatrixManTensor, w_hi: MatrixManTensor, w_lo: MatrixManTensor, k_out: int, c_in: int,
             r: int, s: int, c_pad: int, k_pad: int, bias, stride, padding, dilation, act,
-            residual, residual_before_act, out: MatrixManTensor) -> bool:
+            residual, residual_before_act, out: MatrixManTensor, tile_cap=_FROM_CONFIG) -> bool:
     """tcgen05 3xTF32 convolution on prepacked hi/lo weight planes.
 
     Returns False (nothing launched) when the geometry or layout is outside
-    what the tensor-core kernel covers; the caller then runs mm_conv2d."""
+    what the tensor-core kernel covers; the caller then runs mm_conv2d.  An
+    output larger than the tile cap (conv_tile_cap) runs as several region
+    launches with the same result."""
     params = _lib.MMConvParams(stride[0], stride[1], padding[0], padding[1], dilation[0], dilation[1],
                                1, int(act), 1 if residual_before_act else 0, 2)
-    res_desc = residual.desc() if residual is not None else None
-    name = "mm_conv2d_tc"
     lib = _lib_handle()
     stream = x.runtime.stream
     activate_stream(stream)
-    token = profiling.launch_times.begin(name, stream) if profiling.gpu_timing_enabled() else None
-    status = lib.mm_conv2d_tc(_p(x.desc()), ctypes.c_void_p(w_hi.element_ptr),
-                              ctypes.c_void_p(w_lo.element_ptr), int(k_out), int(c_in), int(r), int(s),
-                              int(c_pad), int(k_pad),
-                              ctypes.c_void_p(bias.element_ptr) if bias is not None else None,
-                              _p(res_desc) if res_desc is not None else None, ctypes.byref(params),
-                              _p(out.desc()), stream)
-    if status == _lib.MM_ERR_UNSUPPORTED:
+    bias_ptr = ctypes.c_void_p(bias.element_ptr) if bias is not None else None
+    oh, ow = int(out.shape[2]), int(out.shape[3])
+    regions = conv_regions(oh, ow, conv_tile_cap(tile_cap))
+    for i, (r0, c0, rows, cols) in enumerate(regions):
+        whole = len(regions) == 1
+        y = out if whole else _region_view(out, r0, c0, rows, cols)
+        res = residual if whole or residual is None else _region_view(residual, r0, c0, rows, cols)
+        res_desc = res.desc() if res is not None else None
+        name = "mm_conv2d_tc" if whole else "mm_conv2d_tc_region"
+        token = profiling.launch_times.begin(name, stream) if profiling.gpu_timing_enabled() else None
+        args = (_p(x.desc()), ctypes.c_void_p(w_hi.element_ptr), ctypes.c_void_p(w_lo.element_ptr),
+                int(k_out), int(c_in), int(r), int(s), int(c_pad), int(k_pad), bias_ptr,
+                _p(res_desc) if res_desc is not None else None, ctypes.byref(params))
+        if whole:
+            status = lib.mm_conv2d_tc(*args, _p(y.desc()), stream)
+        else:
+            status = lib.mm_conv2d_tc_region(*args, ctypes.c_int64(r0), ctypes.c_int64(c0), _p(y.desc()),
+                                             stream)
+        if status == _lib.MM_ERR_UNSUPPORTED and i == 0:
+            if token is not None:
+                profiling.launch_times.end(token)
+                profiling.launch_times.records.pop()
+            return False
+        _lib.check(status, name)
         if token is not None:
             profiling.launch_times.end(token)
-            profiling.launch_times.records.pop()
-        return False
-    _lib.check(status, name)
-    if token is not None:
-        profiling.launch_times.end(token)
-    profiling.count_launch(name)
+        profiling.count_launch(name)
     if config.cudaDisableAsyncQueue or config.cudaDebug:
         x.runtime.synchronize()
         check_kernel_error(x.runtime.index)
