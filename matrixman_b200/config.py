@@ -25,11 +25,13 @@ B200 meaning of the north-star knobs:
   (a positive integer or ``auto``; default 256), and locked after init like
   the other runtime fields.  The reference uses it to bound the physical
   OpenGL tile a convolution renders into (backends/opengl/convolution.py:1299).
-  On CUDA an integer limit bounds the extent of one convolution launch: an
-  output wider or taller than the limit runs as several launches of at most
-  limit x limit output pixels each (mm_conv2d_region / mm_conv2d_tc_region),
-  with the same result bit for bit; ``auto`` means one launch per
-  convolution, whatever its size.
+  On CUDA a limit the user sets (environment or Python) bounds the extent of
+  one convolution launch: an output wider or taller than the limit runs as
+  several launches of at most limit x limit output pixels each
+  (mm_conv2d_region / mm_conv2d_tc_region), with the same result bit for
+  bit.  The default value and ``auto`` mean one launch per convolution,
+  whatever its size, as in the reference's CUDA backend (which never reads
+  the setting).
 
 Settings without a CUDA meaning (OpenGL diagnostics) are accepted and
 reported so that existing scripts keep working; they have no effect.
@@ -57,7 +59,7 @@ _FIELDS: dict[str, tuple] = {
     "useDGPU": (False, "MATRIXMAN_USE_DGPU", "use_dgpu", "Backend / device", "backend-specific",
                 "Requests a discrete adapter (no effect on CUDA)."),
     "tileLimit": (256, "MATRIXMAN_TILE_LIMIT", "tile_limit", "OpenGL tiling", "stable",
-                  "Largest output rows/columns of one convolution launch (auto: no limit)."),
+                  "Largest output rows/columns of one convolution launch when set (default, auto: no limit)."),
     "tileSync": ("per_tile", "MATRIXMAN_TILE_SYNC", "tile_sync", "OpenGL tiling", "stable",
                  "Tiled-convolution synchronization (no effect on CUDA)."),
     "syncPolicy": ("safe", "MATRIXMAN_SYNC_POLICY", "sync_policy", "Synchronization", "stable",

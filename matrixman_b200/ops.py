@@ -356,14 +356,18 @@ def conv_tile_cap(cap=_FROM_CONFIG):
     """Largest output extent (rows and columns) of one convolution launch.
 
     The reference's ``tileLimit`` bounds the physical tile one convolution pass
-    renders into (drivers/matrixman/config.py:305-314, consumed at
-    backends/opengl/convolution.py:1299); on CUDA an integer limit caps each
-    launch at limit x limit output pixels, and ``auto`` means no cap (device
-    buffers have no texture-size limit).  ``cap`` overrides the setting
-    (None: no cap)."""
+    renders into (drivers/matrixman/config.py:305-314, consumed only by the
+    OpenGL convolution, backends/opengl/convolution.py:1299; its CUDA backend
+    runs every convolution as one launch).  Here a limit the user sets (through
+    MATRIXMAN_TILE_LIMIT or a Python override) caps each launch at limit x
+    limit output pixels; the default value (256, reported as in the reference)
+    and ``auto`` keep one launch per convolution, as the reference's CUDA
+    backend does.  ``cap`` overrides the setting (None: no cap)."""
     if cap is _FROM_CONFIG:
         value = config.tileLimit
-        return None if value == "auto" else int(value)
+        if value == "auto" or config.source("tileLimit") == "default":
+            return None
+        return int(value)
     return None if cap is None else int(cap)
 
 

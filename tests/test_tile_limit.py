@@ -32,8 +32,14 @@ def test_one_region_when_uncapped_or_fitting():
 
 
 def test_cap_follows_the_setting_and_its_override():
-    from matrixman_b200.config import config
+    """The default (256, as the reference reports it) and ``auto`` keep one
+    launch per convolution, like the reference's CUDA backend; a value the user
+    sets caps each launch."""
+    from matrixman_b200.config import Configuration, config
     value = config.tileLimit
-    assert ops.conv_tile_cap() == (None if value == "auto" else int(value))
+    explicit = config.source("tileLimit") != "default" and value != "auto"
+    assert ops.conv_tile_cap() == (int(value) if explicit else None)
     assert ops.conv_tile_cap(None) is None
     assert ops.conv_tile_cap(12) == 12
+    cfg = Configuration()
+    assert cfg.tile_limit == 256 and cfg.source("tile_limit") == "default"
