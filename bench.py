@@ -101,6 +101,10 @@ def parse_args():
                    help="run one prepared convolution (SiLU epilogue) on a --batch x C x HW x HW "
                         "input (NCHW for C <= 3, NHWC otherwise) --steps + 1 times, for an ncu "
                         "capture of one kernel")
+    p.add_argument("--conv-sweep", action="store_true",
+                   help="time the tensor-core convolution alone on the YOLOv8n/m 3x3 layer shapes "
+                        "at --batch (default 64): one JSON line per layer with TF/s and the fraction "
+                        "of the 3xTF32 ceiling")
     return p.parse_args()
 
 
@@ -475,6 +479,8 @@ def main():
         return run_profile_case(args)
     if args.profile_conv:
         return run_profile_conv(args)
+    if args.conv_sweep:
+        return run_conv_sweep(args)
     if args.workload == "c1":
         return run_c1(args)
     spec = _specs()[args.workload]
@@ -558,6 +564,50 @@ def run_profile_conv(args):
     matrixman.synchronize()
     print(json.dumps({"profile_conv": [c, k, ks, st, hw], "batch": args.batch,
                       "launches": args.steps + 1, "out": list(y.shape)}))
+
+
+# 3x3 stride-1 layer shapes of YOLOv8n / YOLOv8m at 640 x 640: (C, K, output H = W).
+SWEEP_LAYERS = ((16, 16, 160), (32, 32, 80), (64, 64, 80), (64, 80, 80), (80, 80, 80), (96, 96, 80),
+                (128, 128, 40), (192, 192, 40), (128, 128, 20))
+
+
+def run_conv_sweep(args):
+    """Per-layer throughput of the prepared tensor-core convolution (SiLU
+    epilogue, NHWC input larger than L2 for the 80 x 80 and 160 x 160 layers):
+    CUDA events around 5 back-to-back launches, median of 7."""
+    import torch
+    from torch import nn
+
+    import matrixman_b200 as matrixman
+    from matrixman_b200 import runtime as mrt
+    from matrixman_b200.preparation import PreparedConv2d
+    matrixman.init()
+    matrixman.config.cuda_graphs = False
+    rt = mrt.get_runtime(0)
+    batch = args.batch or 64
+    ceiling = measured_peaks()["bf16_tflops_sustained"] / 6.0
+    g = torch.Generator().manual_seed(7)
+    for c, k, hw in SWEEP_LAYERS:
+        unit = PreparedConv2d(nn.Conv2d(c, k, 3, 1, 1), 2)
+        x = torch.rand(batch, hw, hw, c, generator=g) * 2 - 1
+        xd = matrixman.to_device(x).permute(0, 3, 1, 2)
+        with torch.no_grad():
+            y = unit(xd)
+            rt.synchronize()
+            times = []
+            for _ in range(7):
+                t = mrt.Timer(rt)
+                t.start()
+                for _ in range(5):
+                    y = unit(xd)
+                t.stop()
+                times.append(t.elapsed_ms() / 5)
+        ms = sorted(times)[3]
+        tf = 2.0 * batch * hw * hw * k * c * 9 / (ms * 1e-3) / 1e12
+        print(json.dumps({"conv_sweep": [c, k, 3, hw], "batch": batch, "ms": round(ms, 4),
+                          "tflops": round(tf, 1), "frac_of_3xtf32_ceiling": round(tf / ceiling, 3)}),
+              flush=True)
+        del xd, y
 
 
 def run_reference(args, world, rank):
