@@ -247,14 +247,14 @@ __device__ __forceinline__ float act_fast(float v, int act) {
   return v;
 }
 
-template <int CIN, int R, int S>
+template <int CIN, int R, int S, int KT>
 __global__ void __launch_bounds__(128) conv_smallc_kernel(ConvArgs a, int vec_store) {
   pdl_wait();
-  __shared__ float4 wsm[CIN * R * S * (SC_KT / 4)];
-  const int k0 = blockIdx.y * SC_KT;
-  for (int i = threadIdx.x; i < CIN * R * S * SC_KT; i += blockDim.x) {
-    const int kk = i % SC_KT;
-    const int t = i / SC_KT;  // (c * R + r) * S + s
+  __shared__ float4 wsm[CIN * R * S * (KT / 4)];
+  const int k0 = blockIdx.y * KT;
+  for (int i = threadIdx.x; i < CIN * R * S * KT; i += blockDim.x) {
+    const int kk = i % KT;
+    const int t = i / KT;  // (c * R + r) * S + s
     const int c = t / (R * S), rs = t - c * (R * S);
     const int r = rs / S, s_ = rs - r * S;
     const int k = k0 + kk;
@@ -270,9 +270,33 @@ __global__ void __launch_bounds__(128) conv_smallc_kernel(ConvArgs a, int vec_st
     const int n_ = (int)(q / a.oh);
     const int ih0 = oh_ * a.sh - a.ph, iw0 = ow_ * a.sw - a.pw;
     const float* xb = a.x + (int64_t)n_ * a.xs[0];
-    float acc[SC_KT];
+    float acc[KT];
 #pragma unroll
-    for (int k = 0; k < SC_KT; ++k) acc[k] = 0.f;
+    for (int k = 0; k < KT; ++k) acc[k] = 0.f;
+    // Small windows (at most 48 taps, e.g. 4 channels x 3 x 3): every input
+    // value is loaded before the first FMA, so the loads share one memory
+    // round trip; larger windows (3 x 7 x 7) load as they go.  The FMA order
+    // (channel, row, column) is the same either way.
+    constexpr int TAPS = CIN * R * S;
+    constexpr bool PRELOAD = TAPS <= 48;
+    float xv[PRELOAD ? TAPS : 1];
+    if (PRELOAD) {
+#pragma unroll
+      for (int c = 0; c < CIN; ++c)
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int ih = ih0 + r * a.dh;
+          const bool rok = (unsigned)ih < (unsigned)a.h;
+#pragma unroll
+          for (int s_ = 0; s_ < S; ++s_) {
+            const int iw = iw0 + s_ * a.dw;
+            xv[PRELOAD ? (c * R + r) * S + s_ : 0] =
+                (rok && (unsigned)iw < (unsigned)a.w_in)
+                    ? __ldg(xb + c * a.xs[1] + (int64_t)ih * a.xs[2] + (int64_t)iw * a.xs[3])
+                    : 0.f;
+          }
+        }
+    }
 #pragma unroll
     for (int c = 0; c < CIN; ++c) {
 #pragma unroll
@@ -282,12 +306,13 @@ __global__ void __launch_bounds__(128) conv_smallc_kernel(ConvArgs a, int vec_st
 #pragma unroll
         for (int s_ = 0; s_ < S; ++s_) {
           const int iw = iw0 + s_ * a.dw;
-          const float v = (rok && (unsigned)iw < (unsigned)a.w_in)
+          const float v = PRELOAD ? xv[PRELOAD ? (c * R + r) * S + s_ : 0]
+                          : (rok && (unsigned)iw < (unsigned)a.w_in)
                               ? __ldg(xb + c * a.xs[1] + (int64_t)ih * a.xs[2] + (int64_t)iw * a.xs[3])
                               : 0.f;
-          const float4* wp = wsm + ((c * R + r) * S + s_) * (SC_KT / 4);
+          const float4* wp = wsm + ((c * R + r) * S + s_) * (KT / 4);
 #pragma unroll
-          for (int k4 = 0; k4 < SC_KT / 4; ++k4) {
+          for (int k4 = 0; k4 < KT / 4; ++k4) {
             const float4 w4 = wp[k4];
             acc[4 * k4 + 0] = fmaf(v, w4.x, acc[4 * k4 + 0]);
             acc[4 * k4 + 1] = fmaf(v, w4.y, acc[4 * k4 + 1]);
@@ -300,7 +325,7 @@ __global__ void __launch_bounds__(128) conv_smallc_kernel(ConvArgs a, int vec_st
     const int64_t yb = (int64_t)n_ * a.ys[0] + (int64_t)oh_ * a.ys[2] + (int64_t)ow_ * a.ys[3];
     const int64_t rb = (int64_t)n_ * a.rs[0] + (int64_t)oh_ * a.rs[2] + (int64_t)ow_ * a.rs[3];
 #pragma unroll
-    for (int k = 0; k < SC_KT; ++k) {
+    for (int k = 0; k < KT; ++k) {
       const int kk = min(k0 + k, a.kout - 1);
       float v = acc[k];
       if (a.bias) v += a.bias[kk];
@@ -309,14 +334,14 @@ __global__ void __launch_bounds__(128) conv_smallc_kernel(ConvArgs a, int vec_st
       if (a.res && !a.res_before_act) v += a.res[rb + kk * a.rs[1]];
       acc[k] = v;
     }
-    if (vec_store && k0 + SC_KT <= a.kout) {
+    if (vec_store && k0 + KT <= a.kout) {
       float4* yp = reinterpret_cast<float4*>(a.y + yb + k0);
 #pragma unroll
-      for (int k4 = 0; k4 < SC_KT / 4; ++k4)
+      for (int k4 = 0; k4 < KT / 4; ++k4)
         yp[k4] = make_float4(acc[4 * k4], acc[4 * k4 + 1], acc[4 * k4 + 2], acc[4 * k4 + 3]);
     } else {
 #pragma unroll
-      for (int k = 0; k < SC_KT; ++k)
+      for (int k = 0; k < KT; ++k)
         if (k0 + k < a.kout) a.y[yb + (int64_t)(k0 + k) * a.ys[1]] = acc[k];
     }
   }
@@ -457,8 +482,12 @@ int launch_smallc(const ConvArgs& a, int vec_store, cudaStream_t s) {
   int64_t blocks = (a.m_total + per_block - 1) / per_block;
   const int64_t cap = (int64_t)sm_count() * 16;
   if (blocks > cap) blocks = cap;
-  dim3 grid((unsigned)blocks, (unsigned)((a.kout + SC_KT - 1) / SC_KT));
-  MM_CUDA(launch_pdl(conv_smallc_kernel<CIN, R, S>, grid, dim3(128), 0, s, a, vec_store),
+  // Up to 8 output channels: 8 per thread, half the weight reads and FMAs of
+  // the 16-channel instantiation (same per-output order, same results).
+  const int kt = a.kout <= 8 ? 8 : SC_KT;
+  dim3 grid((unsigned)blocks, (unsigned)((a.kout + kt - 1) / kt));
+  MM_CUDA(kt == 8 ? launch_pdl(conv_smallc_kernel<CIN, R, S, 8>, grid, dim3(128), 0, s, a, vec_store)
+                  : launch_pdl(conv_smallc_kernel<CIN, R, S, SC_KT>, grid, dim3(128), 0, s, a, vec_store),
           "mm_conv2d small-channel launch");
   MM_LAUNCH_CHECK("mm_conv2d small-channel launch");
   return MM_OK;
